@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""SAGA Atop-N decode-attention benchmark (one process per GPU).
+
+Default workload (config 2): one attention layer of a SAGA model, batch 8,
+context 32768, 12 query heads, 1 key head, 2 value heads, head_dim 128,
+N = 512, bf16 KV cache. One step = one amortized Atop-N decode step:
+append of the new token, logits over the reduced key head, threshold
+transform, selection and the sparse V gather, as a single fused kernel.
+
+  value      decode tokens/s of the layer, whole job (sum over ranks): B * N_gpus / step time
+  e2e        the same through the public API (saga_b200.ops.atopn_decode) with
+             the step's inputs copied from pinned host memory and its output
+             copied back, inside the timed region
+  roofline   algorithmic HBM bytes of one step / step time, against the
+             measured copy bandwidth (MEASURED_PEAKS.json)
+
+Inputs are synthetic (seeded, on the device); 4 rotating KV-cache copies
+(4 x 192 MiB > L2) so that no step reads a cache that is still in L2.
+
+--impl reference times the CPU oracle of the reference's algorithm (numpy
+port; the reference itself is Python and cannot run on the GPU box) on
+bounded samples of the same workload, on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+WORKLOADS = {
+    # name: (B, L, Hq, Hk, Hv, D, N, plant)
+    "config2": (8, 32768, 12, 1, 2, 128, 512, 64),
+    "config4": (1, 131072, 12, 1, 2, 128, 1024, 256),
+    "config3_layer": (16, 16384 + 128, 15, 1, 5, 64, 256, 64),
+    "config5_layer": (64, 65536 + 64, 12, 1, 4, 128, 512, 128),
+}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="saga_b200", choices=["saga_b200", "reference"])
+    ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    ap.add_argument("--mode", default="atopn", choices=["atopn", "dense", "calibrate"])
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons (read-only)."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str, enabled=True):
+        self.gpu_id, self.enabled, self.proc, self.path = gpu_id, enabled, None, None
+
+    def start(self):
+        if not self.enabled:
+            return
+        import tempfile
+        self.path = tempfile.mktemp(suffix=".csv")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        with open(self.path) as f:
+            for ln in f:
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) == 7:
+                    try:
+                        rows.append((float(parts[0]), float(parts[1]), parts[3:]))
+                    except ValueError:
+                        pass
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, x in enumerate(r) if x.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_device_inputs(torch, shape, device, seed):
+    """Seeded synthetic tensors on the device: q0, q1, K, V, k_new, v_new."""
+    B, L, Hq, Hk, Hv, D, N, plant = shape
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    bf = torch.bfloat16
+    s = 0.5
+    q0 = torch.randn(B, Hq, 1, D, generator=g, device=device) * s
+    q1 = 0.9 * q0 + math.sqrt(1 - 0.81) * torch.randn(B, Hq, 1, D, generator=g, device=device) * s
+    k = (torch.randn(B, Hk, L, D, generator=g, device=device) * s)
+    G = Hq // Hk
+    for kk in range(Hk):
+        qh = q0[:, kk * G, 0]
+        qhat = qh / qh.norm(dim=-1, keepdim=True)
+        pos = torch.randint(0, L, (B, plant), generator=g, device=device)
+        k[torch.arange(B, device=device)[:, None], kk, pos] += 4.0 * qhat[:, None, :]
+    k = k.to(bf)
+    v = torch.empty(B, Hv, L, D, device=device, dtype=bf)
+    for h in range(Hv):  # chunked to keep the fp32 temporary small
+        v[:, h] = (torch.randn(B, L, D, generator=g, device=device) * s).to(bf)
+    kn = (torch.randn(B, Hk, 1, D, generator=g, device=device) * s).to(bf)
+    vn = (torch.randn(B, Hv, 1, D, generator=g, device=device) * s).to(bf)
+    return q0.to(bf), q1.to(bf), k, v, kn, vn
+
+
+def algorithmic_bytes(shape, union_rows: int, mode: str) -> int:
+    """HBM bytes one step must move (bf16): the key cache, the value rows the
+    step needs, q, out, the appended token and the per-row thresholds."""
+    B, L, Hq, Hk, Hv, D, N, _ = shape
+    e = 2
+    kv = B * Hk * L * D * e
+    if mode == "dense":
+        vb = B * Hv * L * D * e
+    else:
+        vb = union_rows * D * e
+    return kv + vb + 2 * B * Hq * D * e + 2 * B * (Hk + Hv) * D * e + B * Hq * 4
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference's algorithm)
+# ---------------------------------------------------------------------------
+
+def cpu_baseline(shape, steps: int, budget_s: float = 20.0):
+    """Time the numpy oracle's amortized step on one sequence of the workload."""
+    import numpy as np
+    from oracle import atopn_oracle as O
+    from saga_b200.workloads import DecodeShape, make_inputs
+    B, L, Hq, Hk, Hv, D, N, plant = shape
+    sh = DecodeShape(B=1, L=L, Hq=Hq, Hk=Hk, Hv=Hv, D=D, N=N, dtype="bf16", scale=0.5, plant=plant)
+    inp = make_inputs(sh, seed=7)
+    cal = O.atopn_calibrate(inp.q0, inp.k, inp.v, N, "bf16")
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        O.atopn_amortized(inp.q1, inp.k, inp.v, cal["thr"], N, "bf16")
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    t = statistics.median(times)
+    cores = os.cpu_count() or 1
+    return {"value": 1.0 / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"1 of {B} sequences of the workload per step, {len(times)} steps, median {t * 1e3:.1f} ms; "
+                      f"numpy oracle (BLAS threads up to {cores} for the logits GEMM, other ops 1 thread)"}
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+
+def main():
+    args = parse()
+    shape = WORKLOADS[args.workload]
+    B, L, Hq, Hk, Hv, D, N, _ = shape
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {"workload": f"{args.workload}: one SAGA attention layer, batch {B}, context {L}, "
+                          f"Hq {Hq} / Hk {Hk} / Hv {Hv}, head_dim {D}, N {N}, mode {args.mode}",
+              "batch_per_gpu": B, "seq_len": L, "heads": [Hq, Hk, Hv], "head_dim": D, "top_n": N,
+              "parallelism": f"replicas x{world} (batch-sharded, no collective)",
+              "l2": "rotating KV-cache copies, each step reads a cache not in L2"}
+    metric = "decode tokens/s of one Atop-N attention layer (config 2 shapes)"
+    unit = "tokens/s"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(shape, args.steps, budget_s=max(20.0, 0.5 * args.steps))
+        line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config, "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch
+    import torch.distributed as dist
+    from saga_b200 import ops
+    from saga_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    copies = 4 if (B * Hk * L * D * 2) < 2 * L2_BYTES else 1
+    caches = [make_device_inputs(torch, shape, dev, seed=1000 * rank + c) for c in range(copies)]
+    q1 = caches[0][1]
+    thrs = []
+    for c in range(copies):
+        q0c, _, kc, vc, _, _ = caches[c]
+        t = torch.zeros(B * Hq, dtype=torch.float32, device=dev)
+        ops.atopn_calibrate(q0c, kc, vc, None, t, N)
+        thrs.append(t)
+    torch.cuda.synchronize()
+
+    # union of the value rows the step needs (for the algorithmic bytes)
+    diag = {}
+    ops.atopn_decode(q1, caches[0][2], caches[0][3], None, thrs[0], N, diag=diag)
+    torch.cuda.synchronize()
+    sel = diag["sel_idx"].cpu()
+    cnt = diag["count"].cpu().clamp(max=min(2 * N, L))
+    union = 0
+    Gv = Hq // Hv
+    for b in range(B):
+        for vh in range(Hv):
+            s = set()
+            for h in range(vh * Gv, (vh + 1) * Gv):
+                r = b * Hq + h
+                s.update(sel[r, :int(cnt[r])].tolist())
+            union += len(s)
+    launches_per_step = len(diag["launches"])
+    ops.read_status(dev)
+
+    def step(i, q):
+        _, _, kc, vc, kn, vn = caches[i % copies]
+        if args.mode == "atopn":
+            return ops.atopn_decode(q, kc, vc, None, thrs[i % copies], N, k_new=kn, v_new=vn, append_pos=L - 1)
+        if args.mode == "dense":
+            return ops.dense_decode(q, kc, vc, None, k_new=kn, v_new=vn, append_pos=L - 1)
+        return ops.atopn_calibrate(q, kc, vc, None, thrs[i % copies], N)
+
+    # CUDA graph of one step per cache copy (device timing without host gaps)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            step(i, q1)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(copies):
+                step(i, q1)
+    reps = max(1, math.ceil(args.steps / copies))
+    steps_timed = reps * copies
+
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local_rank)
+    sampler = ClockSampler(gpu_id, enabled=not args.no_clocks)
+    sampler.start()
+    with torch.cuda.stream(stream):
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < 0.5:   # untimed soak so the clocks settle
+            graph.replay()
+            stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / steps_timed
+    tmax = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    ms = float(tmax.item())
+    status = ops.read_status(dev)
+
+    # end to end through the public API with host buffers
+    hq = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, pin_memory=True)
+    hq.copy_(q1.cpu())
+    hkn = caches[0][4].cpu().pin_memory()
+    hvn = caches[0][5].cpu().pin_memory()
+    hout = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, pin_memory=True)
+    h2d = hq.numel() * 2 + hkn.numel() * 2 + hvn.numel() * 2
+    d2h = hout.numel() * 2
+    ne = max(copies, args.e2e_steps)
+
+    def e2e_step(i):
+        _, _, kc, vc, _, _ = caches[i % copies]
+        qd = hq.to(dev, non_blocking=True)
+        knd = hkn.to(dev, non_blocking=True)
+        vnd = hvn.to(dev, non_blocking=True)
+        if args.mode == "atopn":
+            o = ops.atopn_decode(qd, kc, vc, None, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
+        elif args.mode == "dense":
+            o = ops.dense_decode(qd, kc, vc, None, k_new=knd, v_new=vnd, append_pos=L - 1)
+        else:
+            o = ops.atopn_calibrate(qd, kc, vc, None, thrs[i % copies], N)
+        hout.copy_(o, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(ne):
+        e2e_step(i)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = torch.tensor([f0.elapsed_time(f1) / ne], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+    ms_e2e = float(ms_e2e.item())
+
+    peak, peak_kind = measured_peaks()
+    abytes = algorithmic_bytes(shape, union, args.mode)
+    achieved = abytes / (ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "frac_of_8TBs_nominal": round(achieved / 8000.0, 4),
+                "traffic": None, "algorithmic_bytes_per_step": abytes,
+                "kernel": "saga_decode_kernel<amortized>" if args.mode == "atopn" else f"saga_decode_kernel<{args.mode}>"}
+    if rank == 0:
+        line = {"metric": metric, "value": round(B * world / (ms * 1e-3), 1), "unit": unit, "n_gpus": world,
+                "steps": steps_timed, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+                "us_per_layer_step": round(ms * 1e3, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": config,
+                "e2e": {"value": round(B * world / (ms_e2e * 1e-3), 1), "unit": unit, "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 5)},
+                "roofline": roofline, "clocks": clocks,
+                "gpu_launches": steps_timed * launches_per_step,
+                "kernels_per_step": diag["launches"], "status": status,
+                "value_rows_union_per_step": union}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(shape, steps=3)
+        print(json.dumps(line))
+    if world > 1:
+        del graph
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,983 @@
+// Fused SAGA decode attention on sm_100a: one persistent kernel per step.
+//
+// Work item = (group g = batch x key head, chunk j of the sequence). The C
+// chunks of a group run concurrently (cooperative launch, static round-robin
+// assignment) and exchange per-chunk statistics through the workspace with
+// bounded group barriers. Per item:
+//   score   the G query heads of the group against the chunk's keys
+//           (reference rounding chain: GEMM -> dtype, * scaling -> dtype,
+//           + mask -> dtype; attention.py:113-128), logits kept in SMEM;
+//   then, by mode:
+//   amortized (attention.py:192-209): tail max over the last 256 logits,
+//           partial exp-sums, logit threshold (136-149), strict selection and
+//           per-chunk counts (triton_atopn.py:42), exclusive prefix of counts
+//           so that at most K = min(2N, L) lowest positions are kept, softmax
+//           weights exp(l - m_chunk) over the kept logits;
+//   calibrate (attention.py:173-189): global max and sum of exp, exact N-th
+//           largest logit by an 8-bit-per-pass radix select over the group,
+//           its probability as the threshold, top-N set (ties by position),
+//           weights = the dtype-rounded probabilities;
+//   dense   (attention.py:64-85): weights exp(l - m_chunk) for all positions;
+//   then the V gather of every needed row once per value head, fp32
+//   accumulation, partial (m, l, o[D]) per head, and a merge split across the
+//   group's chunks.
+#include <algorithm>
+#include <cstdio>
+#include <string>
+
+#include "common.cuh"
+#include "decode_internal.h"
+
+namespace saga {
+
+// ---------------------------------------------------------------------------
+// small SMEM struct for per-head values
+// ---------------------------------------------------------------------------
+struct Misc {
+  float m[kMaxG];      // tail max / global max
+  float t[kMaxG];      // logit threshold / N-th logit
+  float s[kMaxG];      // exp-sum
+  float aux[kMaxG];    // chunk-local stabiliser / p_N
+  int i0[kMaxG];       // prefix / want
+  int i1[kMaxG];       // keep / prefix bits
+  int i2[kMaxG];       // misc
+  int i3[kMaxG];
+  float lsum[kMaxG];
+  int flag;
+  int last;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Scoring (CUDA-core FMA path). 64-position sub-tiles of K are staged in SMEM
+// with cp.async (rows padded by 16 B: conflict-free 16-B reads); thread t
+// scores position t % 64 for the heads of slice t / 64.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, int n,
+                                 const float* __restrict__ qf, float* __restrict__ sc,
+                                 uint8_t* __restrict__ stage) {
+  constexpr int SUB = 64;
+  constexpr int ROWB = D * (int)sizeof(T);
+  constexpr int PITCH = ROWB + 16;
+  constexpr int CPR = ROWB / 16;  // 16-byte pieces per row
+  const int CL = p.CL;
+  const T* kbase = reinterpret_cast<const T*>(p.k) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh;
+  const int nsub = (n + SUB - 1) / SUB;
+  const int h0 = kh * p.G;
+
+  auto issue = [&](int s) {
+    uint8_t* buf = stage + (s & 1) * SUB * PITCH;
+    for (int c = threadIdx.x; c < SUB * CPR; c += kThreads) {
+      const int r = c / CPR, cc = c % CPR;
+      const bool ok = (s * SUB + r) < n;
+      const T* src = kbase + (int64_t)(ok ? (p0 + s * SUB + r) : p0) * p.k_sl + cc * (16 / (int)sizeof(T));
+      cp_async16(buf + r * PITCH + cc * 16, src, ok);
+    }
+    cp_async_commit();
+  };
+
+  const int pos_l = threadIdx.x % SUB;
+  const int slice = threadIdx.x / SUB;  // 0..3
+  const int hps = (p.G + 3) / 4;        // <= 8
+  const int hbeg = slice * hps;
+  const int hend = min(p.G, hbeg + hps);
+
+  issue(0);
+  for (int s = 0; s < nsub; ++s) {
+    if (s + 1 < nsub) {
+      issue(s + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const T* krow = reinterpret_cast<const T*>(stage + (s & 1) * SUB * PITCH + pos_l * PITCH);
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+#pragma unroll 2
+    for (int d = 0; d < D; d += 8) {
+      float kf[8];
+      load8f<T>(krow + d, kf);
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        if (hbeg + hh < hend) {
+          const float* qr = qf + (hbeg + hh) * D + d;
+          const float4 qa = *reinterpret_cast<const float4*>(qr);
+          const float4 qb = *reinterpret_cast<const float4*>(qr + 4);
+          float a = acc[hh];
+          a = fmaf(kf[0], qa.x, a); a = fmaf(kf[1], qa.y, a);
+          a = fmaf(kf[2], qa.z, a); a = fmaf(kf[3], qa.w, a);
+          a = fmaf(kf[4], qb.x, a); a = fmaf(kf[5], qb.y, a);
+          a = fmaf(kf[6], qb.z, a); a = fmaf(kf[7], qb.w, a);
+          acc[hh] = a;
+        }
+      }
+    }
+    const int pl = s * SUB + pos_l;
+    if (pl < n) {
+      const int pos = p0 + pl;
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        const int hl = hbeg + hh;
+        if (hl < hend) {
+          // bmm output in the dtype, then * scaling in fp32 rounded to the
+          // dtype (attention.py:121-122), then + mask (124-126).
+          float l = Num<T>::round(acc[hh]);
+          l = Num<T>::round(__fmul_rn(l, p.scaling));
+          if (p.mask) {
+            const int64_t mo = (int64_t)b * p.m_sb + (int64_t)(h0 + hl) * p.m_sh + (int64_t)pos * p.m_sl;
+            l = Num<T>::round(__fadd_rn(l, mask_value<T>(p.mask, p.mask_dtype, mo)));
+          }
+          sc[hl * CL + pl] = l;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Bit-mask helpers over SMEM words (positions of one head within the chunk).
+// ---------------------------------------------------------------------------
+// Keep only the lowest `r` set bits of w.
+__device__ __forceinline__ uint32_t keep_lowest_bits(uint32_t w, int r) {
+  uint32_t outm = 0;
+  for (int i = 0; i < r && w; ++i) {
+    const uint32_t lo = w & (0u - w);
+    outm |= lo;
+    w ^= lo;
+  }
+  return outm;
+}
+
+// Warp-wide: trim bits[0..nw) to their first `keep` set bits (ascending).
+__device__ void warp_trim_bits(uint32_t* bits, int nw, int keep) {
+  const int lane = threadIdx.x & 31;
+  int running = 0;
+  for (int w0 = 0; w0 < nw; w0 += 32) {
+    const int w = w0 + lane;
+    const uint32_t v = (w < nw) ? bits[w] : 0u;
+    const int c = __popc(v);
+    const int incl = warp_incl_scan(c);
+    const int before = running + incl - c;
+    uint32_t nv = v;
+    if (before >= keep) nv = 0u;
+    else if (before + c > keep) nv = keep_lowest_bits(v, keep - before);
+    if (w < nw) bits[w] = nv;
+    running += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  __syncwarp();
+}
+
+// Warp-wide: write the set positions of bits (ascending) to dst[offset + ...].
+__device__ void warp_write_positions(const uint32_t* bits, int nw, int p0, int* dst, int limit) {
+  const int lane = threadIdx.x & 31;
+  int running = 0;
+  for (int w0 = 0; w0 < nw; w0 += 32) {
+    const int w = w0 + lane;
+    uint32_t v = (w < nw) ? bits[w] : 0u;
+    const int c = __popc(v);
+    const int incl = warp_incl_scan(c);
+    int o = running + incl - c;
+    while (v) {
+      const int bit = __ffs(v) - 1;
+      v &= v - 1;
+      if (o < limit) dst[o] = p0 + w * 32 + bit;
+      ++o;
+    }
+    running += __shfl_sync(0xffffffffu, incl, 31);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// V gather of one item: for each value head of the group, every position with
+// a non-zero weight for at least one of its query heads is read once; weights
+// w[hl][pos] (0 = not selected) multiply the row; fp32 accumulation per warp,
+// then a fixed-order reduction over warps. Writes partial o[D] and l = sum w.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
+                            const float* __restrict__ w, const uint32_t* __restrict__ sel,
+                            bool dense, uint32_t* __restrict__ list, float* __restrict__ red,
+                            float* __restrict__ part, Misc* misc) {
+  constexpr int EPL = D / 32;
+  constexpr int PS = D + 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, Gv = p.Gv, CL = p.CL, nw = (n + 31) / 32;
+  const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
+
+  // l = sum of weights per head (fixed order).
+  for (int hl = warp; hl < G; hl += kWarps) {
+    float s = 0.f;
+    for (int i = lane; i < n; i += 32) s += w[hl * CL + i];
+    s = warp_sum(s);
+    if (lane == 0) misc->lsum[hl] = s;
+  }
+
+  for (int vh = vh_lo; vh <= vh_hi; ++vh) {
+    const int a = max(h0, vh * Gv) - h0;
+    const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
+    const T* vbase = reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh +
+                     (int64_t)p0 * p.v_sl + lane * EPL;
+    for (int hb = a; hb < bnd; hb += 8) {
+      const int nh = min(8, bnd - hb);
+      int cnt;
+      if (!dense) {
+        // compact the union of the heads' selections into list (warp 0)
+        if (warp == 0) {
+          int running = 0;
+          for (int w0 = 0; w0 < nw; w0 += 32) {
+            const int ww = w0 + lane;
+            uint32_t u = 0;
+            if (ww < nw)
+              for (int hh = 0; hh < nh; ++hh) u |= sel[(hb + hh) * (CL / 32) + ww];
+            const int c = __popc(u);
+            const int incl = warp_incl_scan(c);
+            int o = running + incl - c;
+            while (u) {
+              const int bit = __ffs(u) - 1;
+              u &= u - 1;
+              uint32_t hm = 0;
+              for (int hh = 0; hh < nh; ++hh)
+                hm |= ((sel[(hb + hh) * (CL / 32) + ww] >> bit) & 1u) << hh;
+              list[o++] = (uint32_t)(ww * 32 + bit) | (hm << 16);
+            }
+            running += __shfl_sync(0xffffffffu, incl, 31);
+          }
+          if (lane == 0) misc->flag = running;
+        }
+        __syncthreads();
+        cnt = misc->flag;
+      } else {
+        cnt = n;
+      }
+
+      float acc[8][EPL];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
+
+      const uint32_t all = (1u << nh) - 1u;
+      // 4 rows in flight per warp
+      for (int e0 = warp; e0 < cnt; e0 += 4 * kWarps) {
+        float vf[4][EPL];
+        int posv[4];
+        uint32_t hmv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int e = e0 + u * kWarps;
+          if (e < cnt) {
+            const uint32_t ent = dense ? ((uint32_t)e | (all << 16)) : list[e];
+            posv[u] = ent & 0xFFFFu;
+            hmv[u] = ent >> 16;
+            loadNf<T, EPL>(vbase + (int64_t)posv[u] * p.v_sl, vf[u]);
+          } else {
+            posv[u] = 0;
+            hmv[u] = 0;
+#pragma unroll
+            for (int i = 0; i < EPL; ++i) vf[u][i] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+#pragma unroll
+          for (int hh = 0; hh < 8; ++hh) {
+            if ((hmv[u] >> hh) & 1u) {
+              const float ww = w[(hb + hh) * CL + posv[u]];
+#pragma unroll
+              for (int i = 0; i < EPL; ++i) acc[hh][i] = fmaf(ww, vf[u][i], acc[hh][i]);
+            }
+          }
+        }
+      }
+      // cross-warp reduction (fixed order)
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh)
+        if (hh < nh)
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) red[(warp * 8 + hh) * D + lane * EPL + i] = acc[hh][i];
+      __syncthreads();
+      for (int o = threadIdx.x; o < nh * D; o += kThreads) {
+        const int hh = o / D, d = o % D;
+        float s = 0.f;
+#pragma unroll
+        for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
+        part[(hb + hh) * PS + 4 + d] = s;
+      }
+      __syncthreads();
+    }
+  }
+  // m and l of each head
+  for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+    part[hl * PS + 0] = misc->aux[hl];
+    part[hl * PS + 1] = misc->lsum[hl];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Merge of the group's partials: chunk j produces outputs [lo, hi) of the
+// flattened (local head, d) space. Fixed-order sums.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int MODE>
+__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, float* scratch,
+                            Misc* misc) {
+  constexpr int PS = D + 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, C = p.C;
+  const int tot = G * D;
+  const int per = (tot + C - 1) / C;
+  const int lo = j * per, hi = min(tot, lo + per);
+  if (lo >= hi) return;
+  const int hl0 = lo / D, hl1 = (hi - 1) / D;
+  const int nhs = hl1 - hl0 + 1;
+  const float* pg = p.partials + (size_t)g * C * G * PS;
+  float* scl = scratch;  // [nhs][C]
+  // scale factors e^{m_j - M} and the denominators, one warp per head
+  for (int hh = warp; hh < nhs; hh += kWarps) {
+    const int hl = hl0 + hh;
+    float M = -INFINITY;
+    for (int c = lane; c < C; c += 32) M = nanmax(M, __ldcg(&pg[((size_t)c * G + hl) * PS + 0]));
+    M = warp_nanmax(M);
+    float L = 0.f;
+    for (int c = lane; c < C; c += 32) {
+      const float mc = __ldcg(&pg[((size_t)c * G + hl) * PS + 0]);
+      const float f = (MODE == MODE_CALIBRATE) ? 1.f : expf(mc - M);
+      scl[hh * C + c] = f;
+      L += __ldcg(&pg[((size_t)c * G + hl) * PS + 1]) * f;
+    }
+    L = warp_sum(L);
+    if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(L, 1e-12f) : L;
+  }
+  __syncthreads();
+  // lanes per output: a power of two covering C (<= 32)
+  int lpo = 1;
+  while (lpo < C && lpo < 32) lpo <<= 1;
+  const int opw = 32 / lpo;  // outputs per warp pass
+  const int sub = lane / lpo, sl = lane % lpo;
+  for (int o0 = lo + warp * opw; o0 < hi; o0 += kWarps * opw) {
+    const int o = o0 + sub;
+    float acc = 0.f;
+    int hl = 0, d = 0;
+    if (o < hi) {
+      hl = o / D;
+      d = o % D;
+      const int hh = hl - hl0;
+      for (int c = sl; c < C; c += lpo) acc += __ldcg(&pg[((size_t)c * G + hl) * PS + 4 + d]) * scl[hh * C + c];
+    }
+    for (int off = lpo >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (o < hi && sl == 0) {
+      const float r = acc / misc->lsum[hl - hl0];
+      T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + hl) * p.o_sh + d;
+      *out = Num<T>::from_f(r);
+    }
+  }
+}
+
+// Radix select: warp-parallel search of the bin holding the `want`-th largest
+// key among 256 bins (bin 255 = largest). Returns bin; *above = count in
+// higher bins. Called by a full warp.
+__device__ __forceinline__ int find_bin(const int* hist256, int want, int* above) {
+  const int lane = threadIdx.x & 31;
+  int c[8];
+  int s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = __ldcg(&hist256[255 - lane * 8 - i]);
+    s += c[i];
+  }
+  const int incl = warp_incl_scan(s);
+  const int before = incl - s;
+  int bin = -1, ab = 0;
+  if (before < want && want <= incl) {
+    int cum = before;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (bin < 0) {
+        if (cum + c[i] >= want) {
+          bin = 255 - lane * 8 - i;
+          ab = cum;
+        }
+        cum += c[i];
+      }
+    }
+  }
+  const unsigned bal = __ballot_sync(0xffffffffu, bin >= 0);
+  if (bal == 0) {
+    *above = 0;
+    return 0;
+  }
+  const int src = __ffs(bal) - 1;
+  bin = __shfl_sync(0xffffffffu, bin, src);
+  *above = __shfl_sync(0xffffffffu, ab, src);
+  return bin;
+}
+
+// ---------------------------------------------------------------------------
+// The fused kernel.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int MODE>
+__global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  Misc* misc = reinterpret_cast<Misc*>(smem + p.sm.misc);
+  float* qf = reinterpret_cast<float*>(smem + p.sm.q);
+  float* sc = reinterpret_cast<float*>(smem + p.sm.scores);
+  uint32_t* sel = reinterpret_cast<uint32_t*>(smem + p.sm.sel);
+  uint32_t* eqb = reinterpret_cast<uint32_t*>(smem + p.sm.eq);
+  uint32_t* list = reinterpret_cast<uint32_t*>(smem + p.sm.list);
+  uint8_t* stage = smem + p.sm.stage;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, C = p.C, CL = p.CL;
+  constexpr int PS = D + 4;
+
+  for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
+    const int g = item / C, j = item % C;
+    const int b = g / p.Hk, kh = g % p.Hk, h0 = kh * G;
+    const int p0 = j * CL;
+    const int n = min(p.L - p0, CL);
+    const int nw = (n + 31) / 32;
+    int* ctrl = p.ctrl + (size_t)g * kCtrlInts;
+    ChunkStat* stg = p.stats + (size_t)g * C * G;   // [C][G]
+    ChunkStat* st = stg + (size_t)j * G;
+    const int row0 = b * p.Hq + h0;
+
+    // ---- fused append of the decode token (StaticLayer.update's index_copy_)
+    if (p.k_new && p.append_pos >= p0 && p.append_pos < p0 + n) {
+      const int pos = p.append_pos;
+      const T* src = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.kn_sb + (int64_t)kh * p.kn_sh;
+      T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh +
+               (int64_t)pos * p.k_sl;
+      for (int d = threadIdx.x; d < D; d += kThreads) dst[d] = src[d];
+      if (p.v_new) {
+        const int vh_lo = h0 / p.Gv, vh_hi = (h0 + G - 1) / p.Gv;
+        for (int i = threadIdx.x; i < (vh_hi - vh_lo + 1) * D; i += kThreads) {
+          const int vh = vh_lo + i / D, d = i % D;
+          const T* vs = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.vn_sb + (int64_t)vh * p.vn_sh;
+          T* vd = const_cast<T*>(reinterpret_cast<const T*>(p.v)) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh +
+                  (int64_t)pos * p.v_sl;
+          vd[d] = vs[d];
+        }
+      }
+      __threadfence_block();
+    }
+
+    // ---- query heads of the group -> SMEM (fp32)
+    for (int i = threadIdx.x; i < G * D; i += kThreads) {
+      const int hl = i / D, d = i % D;
+      qf[i] = Num<T>::to_f(reinterpret_cast<const T*>(p.q)[(int64_t)b * p.q_sb + (int64_t)(h0 + hl) * p.q_sh + d]);
+    }
+    __syncthreads();
+
+    // ---- logits of the chunk
+    score_chunk_simt<T, D>(p, b, kh, p0, n, qf, sc, stage);
+
+    if constexpr (MODE == MODE_LOGITS) {
+      T* lo = reinterpret_cast<T*>(p.logits_out);
+      for (int i = threadIdx.x; i < G * n; i += kThreads) {
+        const int hl = i / n, pl = i % n;
+        lo[(int64_t)(row0 + hl) * p.lo_ld + p0 + pl] = Num<T>::from_f(sc[hl * CL + pl]);
+      }
+      __syncthreads();
+      continue;
+    }
+
+    if constexpr (MODE == MODE_AMORTIZED) {
+      const int tail_start = p.L - p.tail;
+      // local max and the chunk's part of the tail max (attention.py:142-143)
+      for (int hl = warp; hl < G; hl += kWarps) {
+        float tm = -INFINITY;
+        for (int i = lane; i < n; i += 32)
+          if (p0 + i >= tail_start) tm = nanmax(tm, sc[hl * CL + i]);
+        tm = warp_nanmax(tm);
+        if (lane == 0) st[hl].tmx = tm;
+      }
+      const int first_tail = tail_start / CL;
+      const bool is_tail = (p0 + n > tail_start);
+      group_barrier(&ctrl[0], C - first_tail, is_tail, p.status, &misc->flag);
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        float m = -INFINITY;
+        for (int c = first_tail; c < C; ++c) m = nanmax(m, __ldcg(&stg[(size_t)c * G + hl].tmx));
+        misc->m[hl] = m;
+      }
+      __syncthreads();
+      // partial s = sum(exp(logits - m)), each step rounded as the reference
+      // does in the dtype (attention.py:145)
+      for (int hl = warp; hl < G; hl += kWarps) {
+        const float m = misc->m[hl];
+        float s = 0.f;
+        for (int i = lane; i < n; i += 32)
+          s += Num<T>::round(expf(Num<T>::round(__fsub_rn(sc[hl * CL + i], m))));
+        s = warp_sum(s);
+        if (lane == 0) st[hl].s = s;
+      }
+      group_barrier(&ctrl[1], C, true, p.status, &misc->flag);
+      // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        float s = 0.f;
+        for (int c = 0; c < C; ++c) s += __ldcg(&stg[(size_t)c * G + hl].s);
+        s = Num<T>::round(s);
+        const float thr = clamp_min_keep_nan(p.thr_in[row0 + hl], 1e-30f);
+        const float t = __fadd_rn(misc->m[hl], logf(__fmul_rn(thr, s)));
+        misc->t[hl] = t;
+        misc->s[hl] = s;
+        if (j == 0) {
+          if (p.logit_thr_out) p.logit_thr_out[row0 + hl] = t;
+          if (!isfinite(t)) set_status(p.status, SAGA_STATUS_NONFINITE_THR);
+        }
+      }
+      __syncthreads();
+      // strict selection x > t (triton_atopn.py:42) and per-chunk counts
+      for (int hl = warp; hl < G; hl += kWarps) {
+        const float t = misc->t[hl];
+        int cnt = 0;
+        for (int w = 0; w < nw; ++w) {
+          const int i = w * 32 + lane;
+          const bool pass = (i < n) && (sc[hl * CL + i] > t);
+          const uint32_t bits = __ballot_sync(0xffffffffu, pass);
+          if (lane == 0) sel[hl * (CL / 32) + w] = bits;
+          cnt += __popc(bits);
+        }
+        if (lane == 0) st[hl].cnt = cnt;
+      }
+      group_barrier(&ctrl[2], C, true, p.status, &misc->flag);
+      // exclusive prefix in chunk order: keep the K lowest passing positions
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        int pre = 0, tot = 0;
+        for (int c = 0; c < C; ++c) {
+          const int cc = __ldcg(&stg[(size_t)c * G + hl].cnt);
+          if (c < j) pre += cc;
+          tot += cc;
+        }
+        const int mine = st[hl].cnt;
+        misc->i0[hl] = pre;
+        misc->i1[hl] = max(0, min(mine, p.buf_k - pre));
+        if (j == 0) {
+          if (p.count_out) p.count_out[row0 + hl] = tot;
+          if (tot > p.buf_k) set_status(p.status, SAGA_STATUS_OVERFLOW);
+          if (tot == 0) set_status(p.status, SAGA_STATUS_EMPTY_ROW);
+        }
+      }
+      __syncthreads();
+      for (int hl = warp; hl < G; hl += kWarps) {
+        if (misc->i1[hl] < st[hl].cnt) warp_trim_bits(sel + hl * (CL / 32), nw, misc->i1[hl]);
+        if (p.sel_idx_out)
+          warp_write_positions(sel + hl * (CL / 32), nw, p0,
+                               p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i0[hl],
+                               max(0, min(misc->i1[hl], p.sel_ld - misc->i0[hl])));
+        // chunk-local stabiliser: max over the kept logits
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += 32)
+          if ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) m = fmaxf(m, sc[hl * CL + i]);
+        m = warp_max(m);
+        if (lane == 0) misc->aux[hl] = m;
+      }
+      __syncthreads();
+      // softmax weights over the kept logits (attention.py:158-159)
+      for (int i = threadIdx.x; i < G * n; i += kThreads) {
+        const int hl = i / n, pl = i % n;
+        const bool k = (sel[hl * (CL / 32) + (pl >> 5)] >> (pl & 31)) & 1u;
+        sc[hl * CL + pl] = k ? expf(sc[hl * CL + pl] - misc->aux[hl]) : 0.f;
+      }
+      __syncthreads();
+      gather_item<T, D>(p, b, h0, p0, n, sc, sel, false, list, reinterpret_cast<float*>(stage),
+                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      group_barrier(&ctrl[3], C, true, p.status, &misc->flag);
+    } else if constexpr (MODE == MODE_CALIBRATE) {
+      constexpr int KB = Num<T>::kKeyBits;
+      constexpr int PASSES = KB / 8;
+      const int nsel = p.buf_k;  // min(N, L)
+      int* hsm = reinterpret_cast<int*>(stage);  // [G][256]
+      int* gh = p.hist + (size_t)g * 4 * G * 256;  // [pass][G][256]
+      // local max
+      for (int hl = warp; hl < G; hl += kWarps) {
+        float mx = -INFINITY;
+        for (int i = lane; i < n; i += 32) mx = nanmax(mx, sc[hl * CL + i]);
+        mx = warp_nanmax(mx);
+        if (lane == 0) st[hl].mx = mx;
+      }
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        misc->i0[hl] = nsel;  // rank wanted within the current prefix
+        misc->i1[hl] = 0;     // key prefix so far
+      }
+      int sync_id = 1;
+      for (int pass = 0; pass < PASSES; ++pass) {
+        const int shift = KB - 8 * (pass + 1);
+        for (int i = threadIdx.x; i < G * 256; i += kThreads) hsm[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < G * n; i += kThreads) {
+          const int hl = i / n, pl = i % n;
+          const uint32_t key = Num<T>::key(sc[hl * CL + pl]);
+          const bool match = (pass == 0) || ((key >> (shift + 8)) == (uint32_t)misc->i1[hl]);
+          if (match) atomicAdd(&hsm[hl * 256 + ((key >> shift) & 255u)], 1);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < G * 256; i += kThreads)
+          if (hsm[i]) atomicAdd(&gh[(size_t)pass * G * 256 + i], hsm[i]);
+        if (pass == 1) {
+          // exp-sum with the global max (attention.py:131-133 softmax)
+          for (int hl = warp; hl < G; hl += kWarps) {
+            const float M = misc->m[hl];
+            float s = 0.f;
+            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(sc[hl * CL + i], M));
+            s = warp_sum(s);
+            if (lane == 0) st[hl].s = s;
+          }
+        }
+        group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
+        if (pass == 0) {
+          for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+            float M = -INFINITY;
+            for (int c = 0; c < C; ++c) M = nanmax(M, __ldcg(&stg[(size_t)c * G + hl].mx));
+            misc->m[hl] = M;
+          }
+        }
+        if (pass == 1) {
+          for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+            float s = 0.f;
+            for (int c = 0; c < C; ++c) s += __ldcg(&stg[(size_t)c * G + hl].s);
+            misc->s[hl] = s;
+          }
+        }
+        // the bin of the wanted rank (one warp per head)
+        for (int hl = warp; hl < G; hl += kWarps) {
+          int above = 0;
+          const int bin = find_bin(gh + (size_t)pass * G * 256 + hl * 256, misc->i0[hl], &above);
+          if (lane == 0) {
+            misc->i0[hl] -= above;
+            misc->i1[hl] = (int)(((uint32_t)misc->i1[hl] << 8) | (uint32_t)bin);
+          }
+        }
+        __syncthreads();
+      }
+      if (PASSES == 1) {
+        // (not reached: 16- and 32-bit keys take 2 or 4 passes)
+      }
+      // N-th largest logit and its probability: the threshold
+      // (attention.py:181-187); softmax output as exp(l - M) / S rounded.
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        const float lN = Num<T>::unkey((uint32_t)misc->i1[hl]);
+        const float pN = Num<T>::round(__fdiv_rn(expf(__fsub_rn(lN, misc->m[hl])), misc->s[hl]));
+        misc->t[hl] = lN;
+        misc->aux[hl] = pN;
+        if (j == 0 && p.thr_out) p.thr_out[row0 + hl] = pN;
+      }
+      __syncthreads();
+      // probabilities; greater / equal bits
+      for (int hl = warp; hl < G; hl += kWarps) {
+        const float M = misc->m[hl], S = misc->s[hl], pN = misc->aux[hl];
+        int cg = 0, ce = 0;
+        for (int w = 0; w < nw; ++w) {
+          const int i = w * 32 + lane;
+          float pr = 0.f;
+          if (i < n) {
+            pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(sc[hl * CL + i], M)), S));
+            sc[hl * CL + i] = pr;
+          }
+          const uint32_t gb = __ballot_sync(0xffffffffu, (i < n) && pr > pN);
+          const uint32_t eb = __ballot_sync(0xffffffffu, (i < n) && pr == pN);
+          if (lane == 0) {
+            sel[hl * (CL / 32) + w] = gb;
+            eqb[hl * (CL / 32) + w] = eb;
+          }
+          cg += __popc(gb);
+          ce += __popc(eb);
+        }
+        if (lane == 0) {
+          st[hl].cnt = cg;
+          st[hl].cnt_eq = ce;
+        }
+      }
+      group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
+      // ties at the N-th probability: the lowest positions fill the set
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        int tot_gt = 0;
+        for (int c = 0; c < C; ++c) tot_gt += __ldcg(&stg[(size_t)c * G + hl].cnt);
+        const int need = max(0, nsel - tot_gt);
+        int eq_pre = 0, pos_pre = 0;
+        for (int c = 0; c < j; ++c) {
+          const int ce = __ldcg(&stg[(size_t)c * G + hl].cnt_eq);
+          pos_pre += __ldcg(&stg[(size_t)c * G + hl].cnt) + max(0, min(ce, need - eq_pre));
+          eq_pre += ce;
+        }
+        misc->i2[hl] = max(0, min(st[hl].cnt_eq, need - eq_pre));  // kept ties here
+        misc->i3[hl] = pos_pre;
+        if (j == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
+        misc->aux[hl] = 0.f;  // no stabiliser: weights are probabilities
+      }
+      __syncthreads();
+      for (int hl = warp; hl < G; hl += kWarps) {
+        warp_trim_bits(eqb + hl * (CL / 32), nw, misc->i2[hl]);
+        for (int w = lane; w < nw; w += 32) sel[hl * (CL / 32) + w] |= eqb[hl * (CL / 32) + w];
+        __syncwarp();
+        if (p.sel_idx_out)
+          warp_write_positions(sel + hl * (CL / 32), nw, p0,
+                               p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
+                               max(0, p.sel_ld - misc->i3[hl]));
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < G * n; i += kThreads) {
+        const int hl = i / n, pl = i % n;
+        if (!((sel[hl * (CL / 32) + (pl >> 5)] >> (pl & 31)) & 1u)) sc[hl * CL + pl] = 0.f;
+      }
+      __syncthreads();
+      gather_item<T, D>(p, b, h0, p0, n, sc, sel, false, list, reinterpret_cast<float*>(stage),
+                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
+    } else {  // MODE_DENSE
+      for (int hl = warp; hl < G; hl += kWarps) {
+        float mx = -INFINITY;
+        for (int i = lane; i < n; i += 32) mx = nanmax(mx, sc[hl * CL + i]);
+        mx = warp_nanmax(mx);
+        if (lane == 0) misc->aux[hl] = mx;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < G * n; i += kThreads) {
+        const int hl = i / n, pl = i % n;
+        sc[hl * CL + pl] = expf(sc[hl * CL + pl] - misc->aux[hl]);
+      }
+      __syncthreads();
+      gather_item<T, D>(p, b, h0, p0, n, sc, nullptr, true, list, reinterpret_cast<float*>(stage),
+                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      group_barrier(&ctrl[1], C, true, p.status, &misc->flag);
+    }
+
+    // ---- merge of the group's partials, split across its chunks
+    merge_slice<T, D, MODE>(p, g, j, b, h0, reinterpret_cast<float*>(stage), misc);
+
+    // ---- the group's last chunk to finish resets its counters (and histograms)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      misc->last = (atomicAdd(&ctrl[kCtrlDone], 1) == C - 1);
+    }
+    __syncthreads();
+    if (misc->last) {
+      for (int i = threadIdx.x; i < kCtrlInts; i += kThreads) ctrl[i] = 0;
+      if (MODE == MODE_CALIBRATE) {
+        int* gh = p.hist + (size_t)g * 4 * G * 256;
+        for (int i = threadIdx.x; i < 4 * G * 256; i += kThreads) gh[i] = 0;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: plan and launch
+// ---------------------------------------------------------------------------
+namespace {
+
+struct DevInfo {
+  int sms = 0;
+  int smem_optin = 0;
+};
+
+DevInfo dev_info() {
+  static thread_local int cached_dev = -1;
+  static thread_local DevInfo info;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cached_dev = dev;
+  }
+  return info;
+}
+
+int esize_of(int dt) { return dt == SAGA_FP32 ? 4 : 2; }
+
+template <typename T, int D, int MODE>
+const void* kernel_ptr() {
+  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE>);
+}
+
+const void* pick_kernel(int dt, int D, int mode) {
+#define SAGA_PICK(T)                                                         \
+  if (D == 64) {                                                             \
+    switch (mode) {                                                          \
+      case MODE_AMORTIZED: return kernel_ptr<T, 64, MODE_AMORTIZED>();       \
+      case MODE_CALIBRATE: return kernel_ptr<T, 64, MODE_CALIBRATE>();       \
+      case MODE_DENSE: return kernel_ptr<T, 64, MODE_DENSE>();               \
+      default: return kernel_ptr<T, 64, MODE_LOGITS>();                      \
+    }                                                                        \
+  } else {                                                                   \
+    switch (mode) {                                                          \
+      case MODE_AMORTIZED: return kernel_ptr<T, 128, MODE_AMORTIZED>();      \
+      case MODE_CALIBRATE: return kernel_ptr<T, 128, MODE_CALIBRATE>();      \
+      case MODE_DENSE: return kernel_ptr<T, 128, MODE_DENSE>();              \
+      default: return kernel_ptr<T, 128, MODE_LOGITS>();                     \
+    }                                                                        \
+  }
+  if (dt == SAGA_BF16) { SAGA_PICK(__nv_bfloat16) }
+  if (dt == SAGA_FP16) { SAGA_PICK(__half) }
+  SAGA_PICK(float)
+#undef SAGA_PICK
+}
+
+const char* mode_name(int mode) {
+  switch (mode) {
+    case MODE_AMORTIZED: return "saga_decode_kernel<amortized>";
+    case MODE_CALIBRATE: return "saga_decode_kernel<calibrate>";
+    case MODE_DENSE: return "saga_decode_kernel<dense>";
+    default: return "saga_decode_kernel<logits>";
+  }
+}
+
+size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+
+}  // namespace
+
+int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err) {
+  const DevInfo di = dev_info();
+  if (di.sms <= 0) {
+    *err = "no CUDA device";
+    return SAGA_ERR_CUDA;
+  }
+  const int G = a->Hq / a->Hk, Gv = a->Hq / a->Hv;
+  const int groups = a->B * a->Hk;
+  const int ntiles = (a->L + kTile - 1) / kTile;
+  const int es = esize_of(a->dtype);
+  // largest chunk (in tiles) whose SMEM carve allows two CTAs per SM
+  const int budget2 = std::min(di.smem_optin, 113 * 1024);
+  int max_tiles = 0;
+  for (int t = 1; t <= ntiles; ++t) {
+    if (smem_layout(G, a->D, t * kTile, es, 4096).total <= budget2) max_tiles = t;
+    else break;
+  }
+  if (max_tiles == 0) {
+    for (int t = 1; t <= ntiles; ++t) {
+      if (smem_layout(G, a->D, t * kTile, es, 4096).total <= di.smem_optin) max_tiles = t;
+      else break;
+    }
+  }
+  if (max_tiles == 0) {
+    *err = "shapes need more shared memory than one CTA has";
+    return SAGA_ERR_UNSUPPORTED;
+  }
+  const int c_fit = (ntiles + max_tiles - 1) / max_tiles;
+  const int target = 2 * di.sms;
+  const int c_par = std::max(1, target / std::max(1, groups));
+  int C = std::max(c_fit, std::min(c_par, ntiles));
+  int tiles = (ntiles + C - 1) / C;
+  C = (ntiles + tiles - 1) / tiles;
+  const int CL = tiles * kTile;
+  const SmemLayout sm = smem_layout(G, a->D, CL, es, C);
+
+  pl->G = G;
+  pl->Gv = Gv;
+  pl->groups = groups;
+  pl->C = C;
+  pl->CL = CL;
+  pl->items = groups * C;
+  pl->smem = sm.total;
+  pl->cooperative = (mode != MODE_LOGITS);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode);
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm.total) != cudaSuccess) {
+    *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(cudaGetLastError());
+    return SAGA_ERR_CUDA;
+  }
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kfn, kThreads, sm.total) != cudaSuccess || nb <= 0) {
+    *err = "occupancy query failed";
+    cudaGetLastError();
+    return SAGA_ERR_CUDA;
+  }
+  const int cap = nb * di.sms;
+  if (pl->cooperative && C > cap) {
+    *err = "a group needs more co-resident CTAs than the device holds";
+    return SAGA_ERR_UNSUPPORTED;
+  }
+  pl->grid = pl->cooperative ? std::min(pl->items, cap) : pl->items;
+
+  const int PS = a->D + 4;
+  pl->ws_ctrl = 0;
+  pl->ws_stats = al256((size_t)groups * kCtrlInts * 4);
+  pl->ws_part = pl->ws_stats + al256((size_t)groups * C * G * sizeof(ChunkStat));
+  pl->ws_hist = pl->ws_part + al256((size_t)groups * C * G * PS * 4);
+  pl->ws_total = pl->ws_hist + (mode == MODE_CALIBRATE ? al256((size_t)groups * 4 * G * 256 * 4) : 0);
+  return SAGA_OK;
+}
+
+int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::string* err,
+                  std::string* launched) {
+  DecodePlan pl;
+  int rc = make_decode_plan(a, mode, &pl, err);
+  if (rc) return rc;
+  if (mode != MODE_LOGITS && (a->workspace == nullptr || a->workspace_bytes < pl.ws_total)) {
+    *err = "workspace missing or smaller than saga_workspace_bytes()";
+    return SAGA_ERR_WORKSPACE;
+  }
+  DecodeParams p{};
+  p.B = a->B; p.Hq = a->Hq; p.Hk = a->Hk; p.Hv = a->Hv; p.D = a->D; p.L = a->L;
+  p.G = pl.G; p.Gv = pl.Gv;
+  p.C = pl.C; p.CL = pl.CL; p.items = pl.items;
+  p.tail = std::min(kTail, a->L);
+  if (mode == MODE_AMORTIZED) p.buf_k = std::min(2 * a->top_n, a->L);
+  else if (mode == MODE_CALIBRATE) p.buf_k = std::min(a->top_n, a->L);
+  else p.buf_k = a->L;
+  p.q = a->q; p.q_sb = a->q_sb; p.q_sh = a->q_sh;
+  p.k = a->k; p.k_sb = a->k_sb; p.k_sh = a->k_sh; p.k_sl = a->k_sl;
+  p.v = a->v; p.v_sb = a->v_sb; p.v_sh = a->v_sh; p.v_sl = a->v_sl;
+  p.mask = a->mask; p.mask_dtype = a->mask_dtype; p.m_sb = a->m_sb; p.m_sh = a->m_sh; p.m_sl = a->m_sl;
+  p.scaling = a->scaling;
+  p.thr_in = a->thr_in; p.thr_out = a->thr_out;
+  p.out = a->out; p.o_sb = a->o_sb; p.o_sh = a->o_sh;
+  p.k_new = a->k_new; p.kn_sb = a->kn_sb; p.kn_sh = a->kn_sh;
+  p.v_new = a->v_new; p.vn_sb = a->vn_sb; p.vn_sh = a->vn_sh;
+  p.append_pos = a->append_pos;
+  p.logit_thr_out = a->logit_thr_out; p.count_out = a->count_out;
+  p.sel_idx_out = a->sel_idx_out; p.sel_ld = a->sel_ld;
+  p.logits_out = a->logits_out; p.lo_ld = a->lo_ld;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  if (mode != MODE_LOGITS) {
+    p.ctrl = reinterpret_cast<int*>(ws + pl.ws_ctrl);
+    p.stats = reinterpret_cast<ChunkStat*>(ws + pl.ws_stats);
+    p.partials = reinterpret_cast<float*>(ws + pl.ws_part);
+    p.hist = mode == MODE_CALIBRATE ? reinterpret_cast<int*>(ws + pl.ws_hist) : nullptr;
+  }
+  p.status = a->status;
+  p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C);
+
+  const void* kfn = pick_kernel(a->dtype, a->D, mode);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = pl.cooperative ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* kargs[] = {&p};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kfn, kargs);
+  if (e != cudaSuccess) {
+    *err = std::string("kernel launch: ") + cudaGetErrorString(e);
+    return SAGA_ERR_CUDA;
+  }
+  if (launched) {
+    if (!launched->empty()) *launched += ",";
+    *launched += mode_name(mode);
+  }
+  return SAGA_OK;
+}
+
+}  // namespace saga
