@@ -297,10 +297,11 @@ def main():
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        graph.replay()
-    e1.record(stream)
+    with torch.cuda.stream(stream):  # replays and events on the same stream
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()

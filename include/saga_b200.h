@@ -106,9 +106,13 @@ typedef enum {
 } saga_op;
 
 /* Bytes of workspace the op needs for these shapes (0 plus an error message if
- * the shapes are invalid). The workspace must be zero-filled once when first
- * allocated; the kernels leave it zeroed after every successful call. After a
- * call that reported SAGA_STATUS_WAIT_TIMEOUT, zero it again. */
+ * the shapes are invalid). A workspace belongs to one op and one set of shapes
+ * (dtype, B, Hq, Hk, Hv, D, L): its layout depends on them. It must be
+ * zero-filled when allocated; each successful call leaves its counters zeroed
+ * again, so later calls with the same shapes can reuse it. Zero it again before
+ * using it for other shapes, and after a call that reported
+ * SAGA_STATUS_WAIT_TIMEOUT. Calls that share a workspace must not overlap on
+ * the GPU (one stream at a time). */
 SAGA_API size_t saga_workspace_bytes(const SagaAttnArgs* args, int32_t op);
 
 /* Steady-state Atop-N decode step. Replaces approx_top_n_attention_amortized

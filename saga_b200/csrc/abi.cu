@@ -82,9 +82,11 @@ int mode_of(int op) {
 int run_attn(const SagaAttnArgs* a, int op, void* stream) {
   g_err.clear();
   g_launched.clear();
-  int rc = check_attn(a, op);
+  int rc = check_shapes(a);
   if (rc) return rc;
-  if (a->B == 0) return SAGA_OK;
+  if (a->B == 0) return SAGA_OK;  // nothing to do; empty tensors may carry NULL pointers
+  rc = check_attn(a, op);
+  if (rc) return rc;
   std::string err;
   rc = saga::launch_decode(a, mode_of(op), reinterpret_cast<cudaStream_t>(stream), &err, &g_launched);
   if (rc) return fail(rc, err);

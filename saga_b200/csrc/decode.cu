@@ -4,9 +4,14 @@
 // chunks of a group run concurrently (cooperative launch, static round-robin
 // assignment) and exchange per-chunk statistics through the workspace with
 // bounded group barriers. Per item:
-//   score   the G query heads of the group against the chunk's keys
-//           (reference rounding chain: GEMM -> dtype, * scaling -> dtype,
-//           + mask -> dtype; attention.py:113-128), logits kept in SMEM;
+//   score   the G query heads of the group against the chunk's keys. For
+//           bf16/fp16: TMA streams 128-position K tiles (128-B swizzle) through
+//           a ring of shared-memory stages; one thread issues tcgen05 UMMAs
+//           (M = 128 positions, N = 16 query-head slots, K = D) into a double
+//           buffered TMEM accumulator; four warps read it back (tcgen05.ld).
+//           For fp32: CUDA-core FMAs. Either way the reference rounding chain
+//           is applied (GEMM -> dtype, * scaling -> dtype, + mask -> dtype;
+//           attention.py:113-128) and the logits stay in shared memory;
 //   then, by mode:
 //   amortized (attention.py:192-209): tail max over the last 256 logits,
 //           partial exp-sums, logit threshold (136-149), strict selection and
@@ -18,41 +23,62 @@
 //           its probability as the threshold, top-N set (ties by position),
 //           weights = the dtype-rounded probabilities;
 //   dense   (attention.py:64-85): weights exp(l - m_chunk) for all positions;
-//   then the V gather of every needed row once per value head, fp32
-//   accumulation, partial (m, l, o[D]) per head, and a merge split across the
-//   group's chunks.
+//   then the V gather: every needed value row is fetched once per value head
+//   with bulk copies into shared memory, weighted in fp32 per query head, and
+//   written as a partial (m, l, o[D]); the group's chunks merge the partials.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
 #include "decode_internal.h"
+#include "tc.cuh"
 
 namespace saga {
 
 // ---------------------------------------------------------------------------
-// small SMEM struct for per-head values
+// per-CTA shared scalars
 // ---------------------------------------------------------------------------
 struct Misc {
+  uint64_t full[kMaxStages];   // K tile landed (TMA complete_tx)
+  uint64_t empty[kMaxStages];  // K stage free again (UMMA commit)
+  uint64_t tfull[2];           // TMEM accumulator ready (UMMA commit)
+  uint64_t tempty[2];          // TMEM accumulator drained (4 epilogue warps)
+  uint64_t vbar;               // value rows landed (bulk copies)
+  uint32_t tmem_slot;
+  int abort;
   float m[kMaxG];      // tail max / global max
   float t[kMaxG];      // logit threshold / N-th logit
   float s[kMaxG];      // exp-sum
   float aux[kMaxG];    // chunk-local stabiliser / p_N
   int i0[kMaxG];       // prefix / want
-  int i1[kMaxG];       // keep / prefix bits
-  int i2[kMaxG];       // misc
+  int i1[kMaxG];       // keep / key prefix
+  int i2[kMaxG];
   int i3[kMaxG];
   float lsum[kMaxG];
+  int gstart[kMaxGatherGroups + 1];  // gather groups: list ranges
+  int gvh[kMaxGatherGroups];
+  int ghb[kMaxGatherGroups];
+  int ngroups;
   int flag;
   int last;
 };
+static_assert(sizeof(Misc) <= 2048, "Misc must fit its 2 KB slot");
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+// Per-thread pipeline positions kept across items (only role threads use theirs).
+struct Ring {
+  uint32_t ps = 0, pph = 0;   // producer stage / phase
+  uint32_t ms = 0, mph = 0;   // UMMA issuer stage / phase
+  uint32_t mb = 0, mbph = 0;  // UMMA issuer TMEM buffer / phase
+  uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
+  uint32_t vph = 0;           // value-row barrier phase (all threads)
+};
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
                "r"(valid ? 16 : 0)
                : "memory");
 }
@@ -62,19 +88,30 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// The reference's rounding chain for one logit (attention.py:121-126).
+template <typename T>
+__device__ __forceinline__ float finalize_logit(const DecodeParams& p, float acc, int b, int h, int pos) {
+  float l = Num<T>::round(acc);
+  l = Num<T>::round(__fmul_rn(l, p.scaling));
+  if (p.mask) {
+    const int64_t mo = (int64_t)b * p.m_sb + (int64_t)h * p.m_sh + (int64_t)pos * p.m_sl;
+    l = Num<T>::round(__fadd_rn(l, mask_value<T>(p.mask, p.mask_dtype, mo)));
+  }
+  return l;
+}
+
 // ---------------------------------------------------------------------------
-// Scoring (CUDA-core FMA path). 64-position sub-tiles of K are staged in SMEM
-// with cp.async (rows padded by 16 B: conflict-free 16-B reads); thread t
-// scores position t % 64 for the heads of slice t / 64.
+// Scoring on CUDA cores (fp32 path). 64-position sub-tiles of K are staged in
+// SMEM with cp.async (rows padded by 16 B); thread t scores position t % 64
+// for the heads of slice t / 64.
 // ---------------------------------------------------------------------------
 template <typename T, int D>
 __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, int n,
-                                 const float* __restrict__ qf, float* __restrict__ sc,
-                                 uint8_t* __restrict__ stage) {
+                                 const float* __restrict__ qf, T* __restrict__ sc, uint8_t* __restrict__ stage) {
   constexpr int SUB = 64;
   constexpr int ROWB = D * (int)sizeof(T);
   constexpr int PITCH = ROWB + 16;
-  constexpr int CPR = ROWB / 16;  // 16-byte pieces per row
+  constexpr int CPR = ROWB / 16;
   const int CL = p.CL;
   const T* kbase = reinterpret_cast<const T*>(p.k) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh;
   const int nsub = (n + SUB - 1) / SUB;
@@ -92,8 +129,8 @@ __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, i
   };
 
   const int pos_l = threadIdx.x % SUB;
-  const int slice = threadIdx.x / SUB;  // 0..3
-  const int hps = (p.G + 3) / 4;        // <= 8
+  const int slice = threadIdx.x / SUB;
+  const int hps = (p.G + 3) / 4;
   const int hbeg = slice * hps;
   const int hend = min(p.G, hbeg + hps);
 
@@ -131,21 +168,10 @@ __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, i
     }
     const int pl = s * SUB + pos_l;
     if (pl < n) {
-      const int pos = p0 + pl;
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh) {
         const int hl = hbeg + hh;
-        if (hl < hend) {
-          // bmm output in the dtype, then * scaling in fp32 rounded to the
-          // dtype (attention.py:121-122), then + mask (124-126).
-          float l = Num<T>::round(acc[hh]);
-          l = Num<T>::round(__fmul_rn(l, p.scaling));
-          if (p.mask) {
-            const int64_t mo = (int64_t)b * p.m_sb + (int64_t)(h0 + hl) * p.m_sh + (int64_t)pos * p.m_sl;
-            l = Num<T>::round(__fadd_rn(l, mask_value<T>(p.mask, p.mask_dtype, mo)));
-          }
-          sc[hl * CL + pl] = l;
-        }
+        if (hl < hend) sc[hl * CL + pl] = Num<T>::from_f(finalize_logit<T>(p, acc[hh], b, h0 + hl, p0 + pl));
       }
     }
     __syncthreads();
@@ -153,9 +179,142 @@ __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, i
 }
 
 // ---------------------------------------------------------------------------
+// Scoring on the tensor cores (bf16 / fp16).
+//   warp 0 lane 0: TMA producer of 128 x D key tiles (ring of ns stages);
+//   warp 1 lane 0: UMMA issuer, D(128 x 16, fp32 in TMEM) = K_tile . Q^T;
+//   warps 4-7    : epilogue, lane = position, 16 columns = query-head slots.
+// The query operand (16 rows, zero padded beyond G) is written into SMEM in the
+// same 128-B swizzled K-major layout the TMA produces for the key tiles.
+// ---------------------------------------------------------------------------
+template <typename T, int D>
+__device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int n, T* __restrict__ sc,
+                               uint8_t* __restrict__ qop, uint8_t* __restrict__ ring, Misc* misc, Ring& rg,
+                               uint32_t tmem_base) {
+  constexpr int KB = D / 64;  // 128-byte K blocks per row
+  constexpr uint32_t TILE_BYTES = 128u * D * 2u;
+  constexpr uint32_t IDESC = umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G, CL = p.CL, NS = p.ns;
+  const int h0 = kh * G;
+  const int ntl = (n + 127) / 128;
+
+  // B operand: query heads of the group as 16 rows x D, swizzled.
+  for (int i = threadIdx.x; i < 16 * (D / 8); i += kThreads) {
+    const int h = i / (D / 8), c8 = i % (D / 8);
+    const int kb = c8 >> 3, c = c8 & 7;
+    alignas(16) T vals[8];
+    const T* src = reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_sb + (int64_t)(h0 + h) * p.q_sh + c8 * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) vals[e] = (h < G) ? src[e] : Num<T>::from_f(0.f);
+    *reinterpret_cast<uint4*>(qop + kb * 2048 + h * 128 + ((c ^ (h & 7)) << 4)) = *reinterpret_cast<uint4*>(vals);
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int t = 0; t < ntl && !misc->abort; ++t) {
+        if (!mbar_wait(&misc->empty[rg.ps], rg.pph ^ 1u, p.status)) {
+          misc->abort = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
+        uint8_t* dst = ring + rg.ps * TILE_BYTES;
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, p0 + t * 128, kh, b, &misc->full[rg.ps]);
+        ++issued;
+        if (++rg.ps == (uint32_t)NS) {
+          rg.ps = 0;
+          rg.pph ^= 1u;
+        }
+      }
+      if (misc->abort) {
+        // drain: the last issued tiles may still be landing
+        uint32_t s = rg.ps, ph = rg.pph;
+        for (int k = 0; k < min(issued, NS); ++k) {
+          if (s == 0) {
+            s = NS - 1;
+            ph ^= 1u;
+          } else {
+            --s;
+          }
+          mbar_wait(&misc->full[s], ph, p.status);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int issued = 0;
+      uint32_t last_b = 0, last_ph = 0;
+      for (int t = 0; t < ntl && !misc->abort; ++t) {
+        if (!mbar_wait(&misc->full[rg.ms], rg.mph, p.status) ||
+            !mbar_wait(&misc->tempty[rg.mb], rg.mbph ^ 1u, p.status)) {
+          misc->abort = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_addr(ring + rg.ms * TILE_BYTES);
+        const uint32_t b0 = smem_addr(qop);
+        const uint32_t dt = tmem_base + rg.mb * 16u;
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(dt, umma_desc_sw128(a0 + kb * 16384 + kk * 32), umma_desc_sw128(b0 + kb * 2048 + kk * 32),
+                     IDESC, (kb | kk) != 0);
+        umma_commit(&misc->empty[rg.ms]);
+        umma_commit(&misc->tfull[rg.mb]);
+        last_b = rg.mb;
+        last_ph = rg.mbph;
+        ++issued;
+        if (++rg.ms == (uint32_t)NS) {
+          rg.ms = 0;
+          rg.mph ^= 1u;
+        }
+        if (++rg.mb == 2u) {
+          rg.mb = 0;
+          rg.mbph ^= 1u;
+        }
+      }
+      // all UMMAs of this item complete before their operands are reused
+      if (issued) mbar_wait(&misc->tfull[last_b], last_ph, p.status);
+    }
+  } else if (warp >= 4) {
+    const int q4 = warp - 4;  // TMEM lane quarter of this warp
+    for (int t = 0; t < ntl; ++t) {
+      bool ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) misc->abort = 1;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[16];
+      tmem_ld16(tmem_base + ((uint32_t)(q4 * 32) << 16) + rg.eb * 16u, r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->tempty[rg.eb]);
+      if (++rg.eb == 2u) {
+        rg.eb = 0;
+        rg.ebph ^= 1u;
+      }
+      const int pl = t * 128 + q4 * 32 + lane;
+      if (pl < n) {
+#pragma unroll
+        for (int hl = 0; hl < 16; ++hl)
+          if (hl < G)
+            sc[hl * CL + pl] = Num<T>::from_f(finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, p0 + pl));
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
 // Bit-mask helpers over SMEM words (positions of one head within the chunk).
 // ---------------------------------------------------------------------------
-// Keep only the lowest `r` set bits of w.
 __device__ __forceinline__ uint32_t keep_lowest_bits(uint32_t w, int r) {
   uint32_t outm = 0;
   for (int i = 0; i < r && w; ++i) {
@@ -185,7 +344,7 @@ __device__ void warp_trim_bits(uint32_t* bits, int nw, int keep) {
   __syncwarp();
 }
 
-// Warp-wide: write the set positions of bits (ascending) to dst[offset + ...].
+// Warp-wide: write the set positions of bits (ascending) to dst[0 .. limit).
 __device__ void warp_write_positions(const uint32_t* bits, int nw, int p0, int* dst, int limit) {
   const int lane = threadIdx.x & 31;
   int running = 0;
@@ -205,43 +364,67 @@ __device__ void warp_write_positions(const uint32_t* bits, int nw, int p0, int* 
   }
 }
 
+__device__ __forceinline__ bool bit_of(const uint32_t* bits, int i) { return (bits[i >> 5] >> (i & 31)) & 1u; }
+
+// Weight of (local head hl, chunk position i) by mode: exp(l - stabiliser),
+// or for calibration the probability rounded to the dtype.
+template <typename T, int MODE>
+__device__ __forceinline__ float weight_of(const T* sc, int CL, const Misc* misc, int hl, int i) {
+  const float l = Num<T>::to_f(sc[hl * CL + i]);
+  if constexpr (MODE == MODE_CALIBRATE)
+    return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, misc->m[hl])), misc->s[hl]));
+  else
+    return expf(l - misc->aux[hl]);
+}
+
 // ---------------------------------------------------------------------------
-// V gather of one item: for each value head of the group, every position with
-// a non-zero weight for at least one of its query heads is read once; weights
-// w[hl][pos] (0 = not selected) multiply the row; fp32 accumulation per warp,
-// then a fixed-order reduction over warps. Writes partial o[D] and l = sum w.
+// V gather of one item. For each value head of the group and each batch of up
+// to 8 of its query heads, the positions any of them selected form a list;
+// their value rows are fetched once with bulk copies (one lane per row) into
+// SMEM, weighted per query head and accumulated in fp32 per warp, then
+// reduced across warps in a fixed order into the partial o[D]; l = sum of the
+// weights; m = the stabiliser.
 // ---------------------------------------------------------------------------
-template <typename T, int D>
-__device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
-                            const float* __restrict__ w, const uint32_t* __restrict__ sel,
-                            bool dense, uint32_t* __restrict__ list, float* __restrict__ red,
-                            float* __restrict__ part, Misc* misc) {
+template <typename T, int D, int MODE>
+__device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n, const T* __restrict__ sc,
+                            const uint32_t* __restrict__ sel, uint32_t* __restrict__ list, uint8_t* __restrict__ work,
+                            float* __restrict__ wbuf, float* __restrict__ part, Misc* misc, Ring& rg) {
   constexpr int EPL = D / 32;
   constexpr int PS = D + 4;
+  constexpr uint32_t ROWB = D * sizeof(T);
+  constexpr bool kDense = (MODE == MODE_DENSE);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, Gv = p.Gv, CL = p.CL, nw = (n + 31) / 32;
+  const int BR = p.sm.br;
   const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
 
-  // l = sum of weights per head (fixed order).
+  // l = sum of the weights per head (fixed order)
   for (int hl = warp; hl < G; hl += kWarps) {
     float s = 0.f;
-    for (int i = lane; i < n; i += 32) s += w[hl * CL + i];
+    for (int i = lane; i < n; i += 32)
+      if (kDense || bit_of(sel + hl * (CL / 32), i)) s += weight_of<T, MODE>(sc, CL, misc, hl, i);
     s = warp_sum(s);
     if (lane == 0) misc->lsum[hl] = s;
   }
 
-  for (int vh = vh_lo; vh <= vh_hi; ++vh) {
-    const int a = max(h0, vh * Gv) - h0;
-    const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
-    const T* vbase = reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh +
-                     (int64_t)p0 * p.v_sl + lane * EPL;
-    for (int hb = a; hb < bnd; hb += 8) {
-      const int nh = min(8, bnd - hb);
-      int cnt;
-      if (!dense) {
-        // compact the union of the heads' selections into list (warp 0)
-        if (warp == 0) {
-          int running = 0;
+  // gather groups (value head, batch of <= 8 query heads) and their lists (warp 0)
+  if (warp == 0) {
+    int ng = 0, pos_total = 0;
+    for (int vh = vh_lo; vh <= vh_hi; ++vh) {
+      const int a = max(h0, vh * Gv) - h0;
+      const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
+      for (int hb = a; hb < bnd && ng < kMaxGatherGroups; hb += 8) {
+        const int nh = min(8, bnd - hb);
+        if (lane == 0) {
+          misc->gstart[ng] = pos_total;
+          misc->gvh[ng] = vh;
+          misc->ghb[ng] = hb | (nh << 16);
+        }
+        if (kDense) {
+          const uint32_t all = (1u << nh) - 1u;
+          for (int i = lane; i < n; i += 32) list[pos_total + i] = (uint32_t)i | (all << 16);
+          pos_total += n;
+        } else {
           for (int w0 = 0; w0 < nw; w0 += 32) {
             const int ww = w0 + lane;
             uint32_t u = 0;
@@ -249,84 +432,92 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
               for (int hh = 0; hh < nh; ++hh) u |= sel[(hb + hh) * (CL / 32) + ww];
             const int c = __popc(u);
             const int incl = warp_incl_scan(c);
-            int o = running + incl - c;
+            int o = pos_total + incl - c;
             while (u) {
               const int bit = __ffs(u) - 1;
               u &= u - 1;
               uint32_t hm = 0;
-              for (int hh = 0; hh < nh; ++hh)
-                hm |= ((sel[(hb + hh) * (CL / 32) + ww] >> bit) & 1u) << hh;
+              for (int hh = 0; hh < nh; ++hh) hm |= ((sel[(hb + hh) * (CL / 32) + ww] >> bit) & 1u) << hh;
               list[o++] = (uint32_t)(ww * 32 + bit) | (hm << 16);
             }
-            running += __shfl_sync(0xffffffffu, incl, 31);
+            pos_total += __shfl_sync(0xffffffffu, incl, 31);
           }
-          if (lane == 0) misc->flag = running;
         }
-        __syncthreads();
-        cnt = misc->flag;
-      } else {
-        cnt = n;
+        ++ng;
       }
+    }
+    if (lane == 0) {
+      misc->gstart[ng] = pos_total;
+      misc->ngroups = ng;
+    }
+  }
+  __syncthreads();
 
-      float acc[8][EPL];
+  const int ngroups = misc->ngroups;
+  for (int gi = 0; gi < ngroups; ++gi) {
+    const int g0 = misc->gstart[gi], g1 = misc->gstart[gi + 1];
+    const int vh = misc->gvh[gi];
+    const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+    const T* vrow0 =
+        reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh + (int64_t)p0 * p.v_sl;
+    float acc[8][EPL];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
+      for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
 
-      const uint32_t all = (1u << nh) - 1u;
-      // 4 rows in flight per warp
-      for (int e0 = warp; e0 < cnt; e0 += 4 * kWarps) {
-        float vf[4][EPL];
-        int posv[4];
-        uint32_t hmv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int e = e0 + u * kWarps;
-          if (e < cnt) {
-            const uint32_t ent = dense ? ((uint32_t)e | (all << 16)) : list[e];
-            posv[u] = ent & 0xFFFFu;
-            hmv[u] = ent >> 16;
-            loadNf<T, EPL>(vbase + (int64_t)posv[u] * p.v_sl, vf[u]);
-          } else {
-            posv[u] = 0;
-            hmv[u] = 0;
-#pragma unroll
-            for (int i = 0; i < EPL; ++i) vf[u][i] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-#pragma unroll
-          for (int hh = 0; hh < 8; ++hh) {
-            if ((hmv[u] >> hh) & 1u) {
-              const float ww = w[(hb + hh) * CL + posv[u]];
-#pragma unroll
-              for (int i = 0; i < EPL; ++i) acc[hh][i] = fmaf(ww, vf[u][i], acc[hh][i]);
-            }
-          }
+    for (int e0 = g0; e0 < g1; e0 += BR) {
+      const int rows = min(BR, g1 - e0);
+      if (warp == 0) {
+        if (lane == 0) mbar_arrive_expect_tx(&misc->vbar, (uint32_t)rows * ROWB);
+        __syncwarp();
+        for (int r = lane; r < rows; r += 32) {
+          const int pos = list[e0 + r] & 0xFFFF;
+          bulk_load(work + (size_t)r * ROWB, vrow0 + (int64_t)pos * p.v_sl, ROWB, &misc->vbar);
         }
       }
-      // cross-warp reduction (fixed order)
-#pragma unroll
-      for (int hh = 0; hh < 8; ++hh)
-        if (hh < nh)
-#pragma unroll
-          for (int i = 0; i < EPL; ++i) red[(warp * 8 + hh) * D + lane * EPL + i] = acc[hh][i];
+      // weights of the batch while the rows land
+      for (int i = threadIdx.x; i < rows * 8; i += kThreads) {
+        const int r = i >> 3, hh = i & 7;
+        const uint32_t ent = list[e0 + r];
+        float wv = 0.f;
+        if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, CL, misc, hb + hh, ent & 0xFFFF);
+        wbuf[i] = wv;
+      }
+      mbar_wait(&misc->vbar, rg.vph, p.status);
+      rg.vph ^= 1u;
       __syncthreads();
-      for (int o = threadIdx.x; o < nh * D; o += kThreads) {
-        const int hh = o / D, d = o % D;
-        float s = 0.f;
+      for (int r = warp; r < rows; r += kWarps) {
+        float vf[EPL];
+        loadNf<T, EPL>(reinterpret_cast<const T*>(work + (size_t)r * ROWB) + lane * EPL, vf);
+        const float4 wa = *reinterpret_cast<const float4*>(wbuf + r * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(wbuf + r * 8 + 4);
+        const float wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-        for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
-        part[(hb + hh) * PS + 4 + d] = s;
+        for (int hh = 0; hh < 8; ++hh)
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) acc[hh][i] = fmaf(wr[hh], vf[i], acc[hh][i]);
       }
       __syncthreads();
     }
+    // cross-warp reduction in a fixed order (work is free again)
+    float* red = reinterpret_cast<float*>(work);
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh)
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) red[(warp * 8 + hh) * D + lane * EPL + i] = acc[hh][i];
+    __syncthreads();
+    for (int o = threadIdx.x; o < nh * D; o += kThreads) {
+      const int hh = o / D, d = o % D;
+      float s = 0.f;
+#pragma unroll
+      for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
+      part[(hb + hh) * PS + 4 + d] = s;
+    }
+    __syncthreads();
   }
-  // m and l of each head
   for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-    part[hl * PS + 0] = misc->aux[hl];
+    part[hl * PS + 0] = (MODE == MODE_CALIBRATE) ? 0.f : misc->aux[hl];
     part[hl * PS + 1] = misc->lsum[hl];
   }
 }
@@ -336,8 +527,7 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
 // flattened (local head, d) space. Fixed-order sums.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int MODE>
-__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, float* scratch,
-                            Misc* misc) {
+__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, float* scratch, Misc* misc) {
   constexpr int PS = D + 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, C = p.C;
@@ -349,27 +539,26 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
   const int nhs = hl1 - hl0 + 1;
   const float* pg = p.partials + (size_t)g * C * G * PS;
   float* scl = scratch;  // [nhs][C]
-  // scale factors e^{m_j - M} and the denominators, one warp per head
   for (int hh = warp; hh < nhs; hh += kWarps) {
     const int hl = hl0 + hh;
     float M = -INFINITY;
     for (int c = lane; c < C; c += 32) M = nanmax(M, __ldcg(&pg[((size_t)c * G + hl) * PS + 0]));
     M = warp_nanmax(M);
-    float L = 0.f;
+    float Ls = 0.f;
     for (int c = lane; c < C; c += 32) {
       const float mc = __ldcg(&pg[((size_t)c * G + hl) * PS + 0]);
       const float f = (MODE == MODE_CALIBRATE) ? 1.f : expf(mc - M);
       scl[hh * C + c] = f;
-      L += __ldcg(&pg[((size_t)c * G + hl) * PS + 1]) * f;
+      Ls += __ldcg(&pg[((size_t)c * G + hl) * PS + 1]) * f;
     }
-    L = warp_sum(L);
-    if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(L, 1e-12f) : L;
+    Ls = warp_sum(Ls);
+    // calibration renormalises by max(sum p, 1e-12) (attention.py:161)
+    if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(Ls, 1e-12f) : Ls;
   }
   __syncthreads();
-  // lanes per output: a power of two covering C (<= 32)
   int lpo = 1;
   while (lpo < C && lpo < 32) lpo <<= 1;
-  const int opw = 32 / lpo;  // outputs per warp pass
+  const int opw = 32 / lpo;
   const int sub = lane / lpo, sl = lane % lpo;
   for (int o0 = lo + warp * opw; o0 < hi; o0 += kWarps * opw) {
     const int o = o0 + sub;
@@ -391,7 +580,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
 }
 
 // Radix select: warp-parallel search of the bin holding the `want`-th largest
-// key among 256 bins (bin 255 = largest). Returns bin; *above = count in
+// key among 256 bins (bin 255 = largest). Returns the bin; *above = count in
 // higher bins. Called by a full warp.
 __device__ __forceinline__ int find_bin(const int* hist256, int want, int* above) {
   const int lane = threadIdx.x & 31;
@@ -432,20 +621,49 @@ __device__ __forceinline__ int find_bin(const int* hist256, int want, int* above
 // ---------------------------------------------------------------------------
 // The fused kernel.
 // ---------------------------------------------------------------------------
-template <typename T, int D, int MODE>
-__global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_constant__ DecodeParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+template <typename T, int D, int MODE, bool TC>
+__global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-aligned base (the 128-B swizzle pattern is taken from address bits)
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   Misc* misc = reinterpret_cast<Misc*>(smem + p.sm.misc);
-  float* qf = reinterpret_cast<float*>(smem + p.sm.q);
-  float* sc = reinterpret_cast<float*>(smem + p.sm.scores);
+  uint8_t* qop = smem + p.sm.qop;
+  float* qf = reinterpret_cast<float*>(smem + p.sm.qop);
+  T* sc = reinterpret_cast<T*>(smem + p.sm.scores);
   uint32_t* sel = reinterpret_cast<uint32_t*>(smem + p.sm.sel);
   uint32_t* eqb = reinterpret_cast<uint32_t*>(smem + p.sm.eq);
   uint32_t* list = reinterpret_cast<uint32_t*>(smem + p.sm.list);
-  uint8_t* stage = smem + p.sm.stage;
+  float* wbuf = reinterpret_cast<float*>(smem + p.sm.wbuf);
+  uint8_t* work = smem + p.sm.work;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, C = p.C, CL = p.CL;
   constexpr int PS = D + 4;
+  Ring rg;
+  uint32_t tmem_base = 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kMaxStages; ++s) {
+      mbar_init(&misc->full[s], 1);
+      mbar_init(&misc->empty[s], 1);
+    }
+    for (int bb = 0; bb < 2; ++bb) {
+      mbar_init(&misc->tfull[bb], 1);
+      mbar_init(&misc->tempty[bb], 4);
+    }
+    mbar_init(&misc->vbar, 1);
+    misc->abort = 0;
+    mbar_fence_init();
+  }
+  if constexpr (TC) {
+    if (warp == 1) tmem_alloc(&misc->tmem_slot, 32);
+    tc_fence_before();
+  }
+  __syncthreads();
+  if constexpr (TC) {
+    tc_fence_after();
+    tmem_base = misc->tmem_slot;
+  }
 
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     const int g = item / C, j = item % C;
@@ -454,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
     const int n = min(p.L - p0, CL);
     const int nw = (n + 31) / 32;
     int* ctrl = p.ctrl + (size_t)g * kCtrlInts;
-    ChunkStat* stg = p.stats + (size_t)g * C * G;   // [C][G]
+    ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G]
     ChunkStat* st = stg + (size_t)j * G;
     const int row0 = b * p.Hq + h0;
 
@@ -476,23 +694,27 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         }
       }
       __threadfence_block();
+      fence_proxy_async_global();  // the appended rows are read back by TMA / bulk copies
     }
-
-    // ---- query heads of the group -> SMEM (fp32)
-    for (int i = threadIdx.x; i < G * D; i += kThreads) {
-      const int hl = i / D, d = i % D;
-      qf[i] = Num<T>::to_f(reinterpret_cast<const T*>(p.q)[(int64_t)b * p.q_sb + (int64_t)(h0 + hl) * p.q_sh + d]);
-    }
-    __syncthreads();
 
     // ---- logits of the chunk
-    score_chunk_simt<T, D>(p, b, kh, p0, n, qf, sc, stage);
+    if constexpr (TC) {
+      __syncthreads();
+      score_chunk_tc<T, D>(p, b, kh, p0, n, sc, qop, work, misc, rg, tmem_base);
+    } else {
+      for (int i = threadIdx.x; i < G * D; i += kThreads) {
+        const int hl = i / D, d = i % D;
+        qf[i] = Num<T>::to_f(reinterpret_cast<const T*>(p.q)[(int64_t)b * p.q_sb + (int64_t)(h0 + hl) * p.q_sh + d]);
+      }
+      __syncthreads();
+      score_chunk_simt<T, D>(p, b, kh, p0, n, qf, sc, work);
+    }
 
     if constexpr (MODE == MODE_LOGITS) {
       T* lo = reinterpret_cast<T*>(p.logits_out);
       for (int i = threadIdx.x; i < G * n; i += kThreads) {
         const int hl = i / n, pl = i % n;
-        lo[(int64_t)(row0 + hl) * p.lo_ld + p0 + pl] = Num<T>::from_f(sc[hl * CL + pl]);
+        lo[(int64_t)(row0 + hl) * p.lo_ld + p0 + pl] = sc[hl * CL + pl];
       }
       __syncthreads();
       continue;
@@ -500,11 +722,11 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
 
     if constexpr (MODE == MODE_AMORTIZED) {
       const int tail_start = p.L - p.tail;
-      // local max and the chunk's part of the tail max (attention.py:142-143)
+      // the chunk's part of the tail max (attention.py:142-143)
       for (int hl = warp; hl < G; hl += kWarps) {
         float tm = -INFINITY;
         for (int i = lane; i < n; i += 32)
-          if (p0 + i >= tail_start) tm = nanmax(tm, sc[hl * CL + i]);
+          if (p0 + i >= tail_start) tm = nanmax(tm, Num<T>::to_f(sc[hl * CL + i]));
         tm = warp_nanmax(tm);
         if (lane == 0) st[hl].tmx = tm;
       }
@@ -523,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         const float m = misc->m[hl];
         float s = 0.f;
         for (int i = lane; i < n; i += 32)
-          s += Num<T>::round(expf(Num<T>::round(__fsub_rn(sc[hl * CL + i], m))));
+          s += Num<T>::round(expf(Num<T>::round(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), m))));
         s = warp_sum(s);
         if (lane == 0) st[hl].s = s;
       }
@@ -549,12 +771,15 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         int cnt = 0;
         for (int w = 0; w < nw; ++w) {
           const int i = w * 32 + lane;
-          const bool pass = (i < n) && (sc[hl * CL + i] > t);
+          const bool pass = (i < n) && (Num<T>::to_f(sc[hl * CL + i]) > t);
           const uint32_t bits = __ballot_sync(0xffffffffu, pass);
           if (lane == 0) sel[hl * (CL / 32) + w] = bits;
           cnt += __popc(bits);
         }
-        if (lane == 0) st[hl].cnt = cnt;
+        if (lane == 0) {
+          st[hl].cnt = cnt;
+          misc->i2[hl] = cnt;
+        }
       }
       group_barrier(&ctrl[2], C, true, p.status, &misc->flag);
       // exclusive prefix in chunk order: keep the K lowest passing positions
@@ -565,7 +790,8 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
           if (c < j) pre += cc;
           tot += cc;
         }
-        const int mine = st[hl].cnt;
+        const int mine = misc->i2[hl];
+        pre = max(0, pre);  // bounds every offset below even if the stats were corrupt
         misc->i0[hl] = pre;
         misc->i1[hl] = max(0, min(mine, p.buf_k - pre));
         if (j == 0) {
@@ -576,44 +802,36 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
       }
       __syncthreads();
       for (int hl = warp; hl < G; hl += kWarps) {
-        if (misc->i1[hl] < st[hl].cnt) warp_trim_bits(sel + hl * (CL / 32), nw, misc->i1[hl]);
-        if (p.sel_idx_out)
+        if (misc->i1[hl] < misc->i2[hl]) warp_trim_bits(sel + hl * (CL / 32), nw, misc->i1[hl]);
+        if (p.sel_idx_out && misc->i0[hl] < p.sel_ld)
           warp_write_positions(sel + hl * (CL / 32), nw, p0,
                                p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i0[hl],
                                max(0, min(misc->i1[hl], p.sel_ld - misc->i0[hl])));
         // chunk-local stabiliser: max over the kept logits
         float m = -INFINITY;
         for (int i = lane; i < n; i += 32)
-          if ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) m = fmaxf(m, sc[hl * CL + i]);
+          if (bit_of(sel + hl * (CL / 32), i)) m = fmaxf(m, Num<T>::to_f(sc[hl * CL + i]));
         m = warp_max(m);
         if (lane == 0) misc->aux[hl] = m;
       }
       __syncthreads();
-      // softmax weights over the kept logits (attention.py:158-159)
-      for (int i = threadIdx.x; i < G * n; i += kThreads) {
-        const int hl = i / n, pl = i % n;
-        const bool k = (sel[hl * (CL / 32) + (pl >> 5)] >> (pl & 31)) & 1u;
-        sc[hl * CL + pl] = k ? expf(sc[hl * CL + pl] - misc->aux[hl]) : 0.f;
-      }
-      __syncthreads();
-      gather_item<T, D>(p, b, h0, p0, n, sc, sel, false, list, reinterpret_cast<float*>(stage),
-                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, sel, list, work, wbuf,
+                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
       group_barrier(&ctrl[3], C, true, p.status, &misc->flag);
     } else if constexpr (MODE == MODE_CALIBRATE) {
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
       const int nsel = p.buf_k;  // min(N, L)
-      int* hsm = reinterpret_cast<int*>(stage);  // [G][256]
+      int* hsm = reinterpret_cast<int*>(work);     // [G][256]
       int* gh = p.hist + (size_t)g * 4 * G * 256;  // [pass][G][256]
-      // local max
       for (int hl = warp; hl < G; hl += kWarps) {
         float mx = -INFINITY;
-        for (int i = lane; i < n; i += 32) mx = nanmax(mx, sc[hl * CL + i]);
+        for (int i = lane; i < n; i += 32) mx = nanmax(mx, Num<T>::to_f(sc[hl * CL + i]));
         mx = warp_nanmax(mx);
         if (lane == 0) st[hl].mx = mx;
       }
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-        misc->i0[hl] = nsel;  // rank wanted within the current prefix
+        misc->i0[hl] = nsel;  // rank wanted within the current key prefix
         misc->i1[hl] = 0;     // key prefix so far
       }
       int sync_id = 1;
@@ -623,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         __syncthreads();
         for (int i = threadIdx.x; i < G * n; i += kThreads) {
           const int hl = i / n, pl = i % n;
-          const uint32_t key = Num<T>::key(sc[hl * CL + pl]);
+          const uint32_t key = Num<T>::key(Num<T>::to_f(sc[hl * CL + pl]));
           const bool match = (pass == 0) || ((key >> (shift + 8)) == (uint32_t)misc->i1[hl]);
           if (match) atomicAdd(&hsm[hl * 256 + ((key >> shift) & 255u)], 1);
         }
@@ -635,7 +853,7 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
           for (int hl = warp; hl < G; hl += kWarps) {
             const float M = misc->m[hl];
             float s = 0.f;
-            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(sc[hl * CL + i], M));
+            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), M));
             s = warp_sum(s);
             if (lane == 0) st[hl].s = s;
           }
@@ -655,7 +873,6 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
             misc->s[hl] = s;
           }
         }
-        // the bin of the wanted rank (one warp per head)
         for (int hl = warp; hl < G; hl += kWarps) {
           int above = 0;
           const int bin = find_bin(gh + (size_t)pass * G * 256 + hl * 256, misc->i0[hl], &above);
@@ -666,11 +883,8 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         }
         __syncthreads();
       }
-      if (PASSES == 1) {
-        // (not reached: 16- and 32-bit keys take 2 or 4 passes)
-      }
-      // N-th largest logit and its probability: the threshold
-      // (attention.py:181-187); softmax output as exp(l - M) / S rounded.
+      // the N-th largest logit; its probability is the threshold
+      // (attention.py:181-187); softmax output exp(l - M) / S rounded.
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         const float lN = Num<T>::unkey((uint32_t)misc->i1[hl]);
         const float pN = Num<T>::round(__fdiv_rn(expf(__fsub_rn(lN, misc->m[hl])), misc->s[hl]));
@@ -679,17 +893,13 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         if (j == 0 && p.thr_out) p.thr_out[row0 + hl] = pN;
       }
       __syncthreads();
-      // probabilities; greater / equal bits
       for (int hl = warp; hl < G; hl += kWarps) {
         const float M = misc->m[hl], S = misc->s[hl], pN = misc->aux[hl];
         int cg = 0, ce = 0;
         for (int w = 0; w < nw; ++w) {
           const int i = w * 32 + lane;
           float pr = 0.f;
-          if (i < n) {
-            pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(sc[hl * CL + i], M)), S));
-            sc[hl * CL + i] = pr;
-          }
+          if (i < n) pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), M)), S));
           const uint32_t gb = __ballot_sync(0xffffffffu, (i < n) && pr > pN);
           const uint32_t eb = __ballot_sync(0xffffffffu, (i < n) && pr == pN);
           if (lane == 0) {
@@ -702,6 +912,7 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
         if (lane == 0) {
           st[hl].cnt = cg;
           st[hl].cnt_eq = ce;
+          misc->i2[hl] = ce;
         }
       }
       group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
@@ -716,50 +927,39 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
           pos_pre += __ldcg(&stg[(size_t)c * G + hl].cnt) + max(0, min(ce, need - eq_pre));
           eq_pre += ce;
         }
-        misc->i2[hl] = max(0, min(st[hl].cnt_eq, need - eq_pre));  // kept ties here
-        misc->i3[hl] = pos_pre;
+        misc->i2[hl] = max(0, min(misc->i2[hl], need - eq_pre));  // kept ties here
+        misc->i3[hl] = max(0, pos_pre);
         if (j == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
-        misc->aux[hl] = 0.f;  // no stabiliser: weights are probabilities
       }
       __syncthreads();
       for (int hl = warp; hl < G; hl += kWarps) {
         warp_trim_bits(eqb + hl * (CL / 32), nw, misc->i2[hl]);
         for (int w = lane; w < nw; w += 32) sel[hl * (CL / 32) + w] |= eqb[hl * (CL / 32) + w];
         __syncwarp();
-        if (p.sel_idx_out)
+        if (p.sel_idx_out && misc->i3[hl] < p.sel_ld)
           warp_write_positions(sel + hl * (CL / 32), nw, p0,
                                p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
                                max(0, p.sel_ld - misc->i3[hl]));
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < G * n; i += kThreads) {
-        const int hl = i / n, pl = i % n;
-        if (!((sel[hl * (CL / 32) + (pl >> 5)] >> (pl & 31)) & 1u)) sc[hl * CL + pl] = 0.f;
-      }
-      __syncthreads();
-      gather_item<T, D>(p, b, h0, p0, n, sc, sel, false, list, reinterpret_cast<float*>(stage),
-                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, sel, list, work, wbuf,
+                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
       group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
     } else {  // MODE_DENSE
       for (int hl = warp; hl < G; hl += kWarps) {
         float mx = -INFINITY;
-        for (int i = lane; i < n; i += 32) mx = nanmax(mx, sc[hl * CL + i]);
+        for (int i = lane; i < n; i += 32) mx = nanmax(mx, Num<T>::to_f(sc[hl * CL + i]));
         mx = warp_nanmax(mx);
         if (lane == 0) misc->aux[hl] = mx;
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < G * n; i += kThreads) {
-        const int hl = i / n, pl = i % n;
-        sc[hl * CL + pl] = expf(sc[hl * CL + pl] - misc->aux[hl]);
-      }
-      __syncthreads();
-      gather_item<T, D>(p, b, h0, p0, n, sc, nullptr, true, list, reinterpret_cast<float*>(stage),
-                        p.partials + ((size_t)g * C + j) * G * PS, misc);
+      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, nullptr, list, work, wbuf,
+                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
       group_barrier(&ctrl[1], C, true, p.status, &misc->flag);
     }
 
     // ---- merge of the group's partials, split across its chunks
-    merge_slice<T, D, MODE>(p, g, j, b, h0, reinterpret_cast<float*>(stage), misc);
+    merge_slice<T, D, MODE>(p, g, j, b, h0, reinterpret_cast<float*>(work), misc);
 
     // ---- the group's last chunk to finish resets its counters (and histograms)
     __syncthreads();
@@ -776,6 +976,14 @@ __global__ void __launch_bounds__(kThreads, 2) saga_decode_kernel(const __grid_c
       }
     }
     __syncthreads();
+  }
+
+  if constexpr (TC) {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, 32);
+    }
   }
 }
 
@@ -804,32 +1012,33 @@ DevInfo dev_info() {
 
 int esize_of(int dt) { return dt == SAGA_FP32 ? 4 : 2; }
 
-template <typename T, int D, int MODE>
-const void* kernel_ptr() {
-  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE>);
+template <typename T, int D, int MODE, bool TC>
+const void* kptr() {
+  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE, TC>);
+}
+
+template <typename T, bool TC>
+const void* pick_d_mode(int D, int mode) {
+  if (D == 64) {
+    switch (mode) {
+      case MODE_AMORTIZED: return kptr<T, 64, MODE_AMORTIZED, TC>();
+      case MODE_CALIBRATE: return kptr<T, 64, MODE_CALIBRATE, TC>();
+      case MODE_DENSE: return kptr<T, 64, MODE_DENSE, TC>();
+      default: return kptr<T, 64, MODE_LOGITS, TC>();
+    }
+  }
+  switch (mode) {
+    case MODE_AMORTIZED: return kptr<T, 128, MODE_AMORTIZED, TC>();
+    case MODE_CALIBRATE: return kptr<T, 128, MODE_CALIBRATE, TC>();
+    case MODE_DENSE: return kptr<T, 128, MODE_DENSE, TC>();
+    default: return kptr<T, 128, MODE_LOGITS, TC>();
+  }
 }
 
 const void* pick_kernel(int dt, int D, int mode) {
-#define SAGA_PICK(T)                                                         \
-  if (D == 64) {                                                             \
-    switch (mode) {                                                          \
-      case MODE_AMORTIZED: return kernel_ptr<T, 64, MODE_AMORTIZED>();       \
-      case MODE_CALIBRATE: return kernel_ptr<T, 64, MODE_CALIBRATE>();       \
-      case MODE_DENSE: return kernel_ptr<T, 64, MODE_DENSE>();               \
-      default: return kernel_ptr<T, 64, MODE_LOGITS>();                      \
-    }                                                                        \
-  } else {                                                                   \
-    switch (mode) {                                                          \
-      case MODE_AMORTIZED: return kernel_ptr<T, 128, MODE_AMORTIZED>();      \
-      case MODE_CALIBRATE: return kernel_ptr<T, 128, MODE_CALIBRATE>();      \
-      case MODE_DENSE: return kernel_ptr<T, 128, MODE_DENSE>();              \
-      default: return kernel_ptr<T, 128, MODE_LOGITS>();                     \
-    }                                                                        \
-  }
-  if (dt == SAGA_BF16) { SAGA_PICK(__nv_bfloat16) }
-  if (dt == SAGA_FP16) { SAGA_PICK(__half) }
-  SAGA_PICK(float)
-#undef SAGA_PICK
+  if (dt == SAGA_BF16) return pick_d_mode<__nv_bfloat16, true>(D, mode);
+  if (dt == SAGA_FP16) return pick_d_mode<__half, true>(D, mode);
+  return pick_d_mode<float, false>(D, mode);
 }
 
 const char* mode_name(int mode) {
@@ -843,6 +1052,35 @@ const char* mode_name(int mode) {
 
 size_t al256(size_t x) { return (x + 255) / 256 * 256; }
 
+// Gather groups of one key-head group: for each value head it touches, one
+// group per batch of <= 8 of its query heads. Sizes the position list.
+int gather_groups_per_group(int Hq, int Hk, int Hv) {
+  const int G = Hq / Hk, Gv = Hq / Hv;
+  int m = 1;
+  for (int kh = 0; kh < Hk; ++kh) {
+    const int h0 = kh * G;
+    int ng = 0;
+    for (int vh = h0 / Gv; vh <= (h0 + G - 1) / Gv; ++vh) {
+      const int nh = std::min(h0 + G, (vh + 1) * Gv) - std::max(h0, vh * Gv);
+      ng += (nh + 7) / 8;
+    }
+    m = std::max(m, ng);
+  }
+  return m;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
 }  // namespace
 
 int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err) {
@@ -855,31 +1093,32 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   const int groups = a->B * a->Hk;
   const int ntiles = (a->L + kTile - 1) / kTile;
   const int es = esize_of(a->dtype);
-  // largest chunk (in tiles) whose SMEM carve allows two CTAs per SM
-  const int budget2 = std::min(di.smem_optin, 113 * 1024);
-  int max_tiles = 0;
-  for (int t = 1; t <= ntiles; ++t) {
-    if (smem_layout(G, a->D, t * kTile, es, 4096).total <= budget2) max_tiles = t;
-    else break;
-  }
-  if (max_tiles == 0) {
+  const bool tc = (a->dtype != SAGA_FP32);
+  const int nvh = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
+  // tensor-core path: one CTA per SM, deepest K ring that fits; fp32: two per SM
+  const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
+  int ns = tc ? kMaxStages : 2, max_tiles = 0;
+  for (; ns >= 2; --ns) {
+    max_tiles = 0;
     for (int t = 1; t <= ntiles; ++t) {
-      if (smem_layout(G, a->D, t * kTile, es, 4096).total <= di.smem_optin) max_tiles = t;
+      if (smem_layout(G, a->D, t * kTile, es, 4096, tc, ns, nvh).total <= budget) max_tiles = t;
       else break;
     }
+    if (!tc || max_tiles >= std::min(ntiles, 8)) break;
   }
+  if (ns < 2) ns = 2;
   if (max_tiles == 0) {
     *err = "shapes need more shared memory than one CTA has";
     return SAGA_ERR_UNSUPPORTED;
   }
   const int c_fit = (ntiles + max_tiles - 1) / max_tiles;
-  const int target = 2 * di.sms;
+  const int target = tc ? di.sms : 2 * di.sms;
   const int c_par = std::max(1, target / std::max(1, groups));
   int C = std::max(c_fit, std::min(c_par, ntiles));
   int tiles = (ntiles + C - 1) / C;
   C = (ntiles + tiles - 1) / tiles;
   const int CL = tiles * kTile;
-  const SmemLayout sm = smem_layout(G, a->D, CL, es, C);
+  const SmemLayout sm = smem_layout(G, a->D, CL, es, C, tc, ns, nvh);
 
   pl->G = G;
   pl->Gv = Gv;
@@ -888,6 +1127,9 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   pl->CL = CL;
   pl->items = groups * C;
   pl->smem = sm.total;
+  pl->ns = ns;
+  pl->nvh = nvh;
+  pl->tc = tc;
   pl->cooperative = (mode != MODE_LOGITS);
   const void* kfn = pick_kernel(a->dtype, a->D, mode);
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm.total) != cudaSuccess) {
@@ -909,10 +1151,10 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
 
   const int PS = a->D + 4;
   pl->ws_ctrl = 0;
-  pl->ws_stats = al256((size_t)groups * kCtrlInts * 4);
+  pl->ws_hist = al256((size_t)groups * kCtrlInts * 4);
+  pl->ws_stats = pl->ws_hist + (mode == MODE_CALIBRATE ? al256((size_t)groups * 4 * G * 256 * 4) : 0);
   pl->ws_part = pl->ws_stats + al256((size_t)groups * C * G * sizeof(ChunkStat));
-  pl->ws_hist = pl->ws_part + al256((size_t)groups * C * G * PS * 4);
-  pl->ws_total = pl->ws_hist + (mode == MODE_CALIBRATE ? al256((size_t)groups * 4 * G * 256 * 4) : 0);
+  pl->ws_total = pl->ws_part + al256((size_t)groups * C * G * PS * 4);
   return SAGA_OK;
 }
 
@@ -925,10 +1167,11 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     *err = "workspace missing or smaller than saga_workspace_bytes()";
     return SAGA_ERR_WORKSPACE;
   }
-  DecodeParams p{};
+  DecodeParams p;
+  memset(&p, 0, sizeof(p));
   p.B = a->B; p.Hq = a->Hq; p.Hk = a->Hk; p.Hv = a->Hv; p.D = a->D; p.L = a->L;
   p.G = pl.G; p.Gv = pl.Gv;
-  p.C = pl.C; p.CL = pl.CL; p.items = pl.items;
+  p.C = pl.C; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
   p.tail = std::min(kTail, a->L);
   if (mode == MODE_AMORTIZED) p.buf_k = std::min(2 * a->top_n, a->L);
   else if (mode == MODE_CALIBRATE) p.buf_k = std::min(a->top_n, a->L);
@@ -949,12 +1192,37 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
   if (mode != MODE_LOGITS) {
     p.ctrl = reinterpret_cast<int*>(ws + pl.ws_ctrl);
+    p.hist = mode == MODE_CALIBRATE ? reinterpret_cast<int*>(ws + pl.ws_hist) : nullptr;
     p.stats = reinterpret_cast<ChunkStat*>(ws + pl.ws_stats);
     p.partials = reinterpret_cast<float*>(ws + pl.ws_part);
-    p.hist = mode == MODE_CALIBRATE ? reinterpret_cast<int*>(ws + pl.ws_hist) : nullptr;
   }
   p.status = a->status;
-  p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C);
+  p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C, pl.tc, pl.ns, pl.nvh);
+
+  if (pl.tc) {
+    auto enc = encode_fn();
+    if (!enc) {
+      *err = "cuTensorMapEncodeTiled unavailable";
+      return SAGA_ERR_CUDA;
+    }
+    const uint64_t es = 2;
+    // strides of size-1 dims do not matter; keep them valid (multiples of 16 B)
+    const uint64_t sl = (uint64_t)a->k_sl * es;
+    const uint64_t sh = a->Hk > 1 ? (uint64_t)a->k_sh * es : sl * (uint64_t)a->L;
+    const uint64_t sb = a->B > 1 ? (uint64_t)a->k_sb * es : sh * (uint64_t)a->Hk;
+    cuuint64_t dims[4] = {(cuuint64_t)a->D, (cuuint64_t)a->L, (cuuint64_t)a->Hk, (cuuint64_t)a->B};
+    cuuint64_t strides[3] = {sl, sh, sb};
+    cuuint32_t box[4] = {64, 128, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(&p.tmap,
+                     a->dtype == SAGA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                     const_cast<void*>(a->k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      *err = "cuTensorMapEncodeTiled failed for the key cache (" + std::to_string((int)r) + ")";
+      return SAGA_ERR_INVALID;
+    }
+  }
 
   const void* kfn = pick_kernel(a->dtype, a->D, mode);
   cudaLaunchConfig_t cfg{};

@@ -1,6 +1,7 @@
 // Host-side plan and parameters of the fused decode kernel (internal).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -26,42 +27,54 @@ struct ChunkStat {
 constexpr int kCtrlInts = 32;   // control counters per group
 constexpr int kCtrlDone = 31;   // index of the group's completion counter
 constexpr int kMaxG = 32;       // query heads per key head supported
+constexpr int kMaxStages = 4;   // K-tile ring depth of the tensor-core scorer
+constexpr int kMaxGatherGroups = 64;
 
-// Shared-memory carve of the fused kernel (bytes from the dynamic base).
+// Shared-memory carve of the fused kernel, in bytes from a 1024-aligned base.
 struct SmemLayout {
-  int misc, q, scores, sel, eq, list, stage, total;
-  int stage_bytes;
+  int misc, qop, scores, sel, eq, list, wbuf, work, total;
+  int work_bytes;  // K-tile ring / SIMT stages, then V rows, histograms, reductions
+  int br;          // value rows per gather batch
 };
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-__host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esize, int C) {
+// G query heads per key head, head dim D, CL positions per chunk, esize bytes
+// per element, C chunks per group, tensor-core scorer with ns stages, nvh
+// value heads per group.
+__host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esize, int C, bool tc, int ns,
+                                                 int nvh) {
   SmemLayout l;
+  const int rowb = D * esize;
+  int work = tc ? ns * 128 * rowb : 2 * 64 * (rowb + 16);
+  const int red = 8 * 8 * D * 4;
+  const int hist = G * 256 * 4;
+  const int merge = (G + 2 * C + 64) * 4 + 256;
+  work = work > red ? work : red;
+  work = work > hist ? work : hist;
+  work = work > merge ? work : merge;
+  work = align_up(work, 1024);
+  int br = work / rowb;
+  br = br > 4096 ? 4096 : br;
   int off = 0;
   l.misc = off;   off += 2048;
-  l.q = off;      off += align_up(G * D * 4, 128);
-  l.scores = off; off += align_up(G * CL * 4, 128);
+  l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
+  l.work = off;   off += work;
+  l.scores = off; off += align_up(G * CL * esize, 128);
   l.sel = off;    off += align_up(G * (CL / 32) * 4, 128);
   l.eq = off;     off += align_up(G * (CL / 32) * 4, 128);
-  l.list = off;   off += align_up(CL * 4, 128);
-  l.stage = off;
-  const int pitch = D * esize + 16;
-  int st = 2 * 64 * pitch;                         // two staged K sub-tiles
-  int red = 8 * 8 * D * 4;                         // gather reduction (8 warps x 8 heads)
-  int hist = G * 256 * 4;                          // radix histogram
-  int merge = (G + 2 * C + 64) * 4 + 64 * 4;       // merge scale factors (bound)
-  st = st > red ? st : red;
-  st = st > hist ? st : hist;
-  st = st > merge ? st : merge;
-  l.stage_bytes = align_up(st, 128);
-  off += l.stage_bytes;
-  l.total = off;
+  l.list = off;   off += align_up(nvh * CL * 4, 128);
+  l.wbuf = off;   off += align_up(br * 8 * 4, 128);
+  l.total = off + 1024;  // slack to align the dynamic base to 1024
+  l.work_bytes = work;
+  l.br = br;
   return l;
 }
 
 struct DecodeParams {
+  CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
   int B, Hq, Hk, Hv, D, L, G, Gv;
-  int C, CL, items, tail, buf_k;
+  int C, CL, items, tail, buf_k, ns, nvh;
   const void* q; int64_t q_sb, q_sh;
   const void* k; int64_t k_sb, k_sh, k_sl;
   const void* v; int64_t v_sb, v_sh, v_sl;
@@ -80,8 +93,8 @@ struct DecodeParams {
 };
 
 struct DecodePlan {
-  int G, Gv, groups, C, CL, items, grid, smem;
-  bool cooperative;
+  int G, Gv, groups, C, CL, items, grid, smem, ns, nvh;
+  bool cooperative, tc;
   size_t ws_ctrl, ws_stats, ws_part, ws_hist, ws_total;
 };
 

@@ -10,7 +10,7 @@ traces through them.
 
 Workspaces come from torch's caching allocator. They are zero-filled when
 created, and each kernel leaves them zeroed. A workspace is cached per
-(device, op), the way the reference caches its buffers
+(device, op, shapes), the way the reference caches its buffers per shape
 (triton_atopn.py:56, 74-84): callers on one device must run on one stream at
 a time.
 """
@@ -79,9 +79,10 @@ def _workspace(args: L.SagaAttnArgs, op: int, device: torch.device) -> torch.Ten
     nbytes = L.lib.saga_workspace_bytes(ctypes.byref(args), op)
     if nbytes == 0:
         raise L.SagaError(L.SAGA_ERR_INVALID, "saga_workspace_bytes")
-    key = (device.index, op)
+    # A workspace's layout depends on the shapes, so one is kept per shape.
+    key = (device.index, op, args.dtype, args.B, args.Hq, args.Hk, args.Hv, args.D, args.L)
     ws = _WORKSPACES.get(key)
-    if ws is None or ws.numel() < nbytes:
+    if ws is None:
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         _WORKSPACES[key] = ws
     return ws

@@ -20,6 +20,7 @@ pytestmark = pytest.mark.gpu
 
 BF16_MAXABS, BF16_RELRMS, FP32_MAXABS = 2e-2, 1e-2, 1e-4
 FP32_LOGIT_TOL = 2e-5
+LOGIT_ABS_TOL = 1e-5  # fp32 accumulation error of a D<=128 dot product near 0
 NAMES = golden_names()
 
 
@@ -90,7 +91,8 @@ def test_logits(gold, name):
     else:
         d = lg != ref
         assert d.mean() < 1e-3
-        assert np.all(np.abs(lg - ref)[d] <= 2 * ulp(ref[d], dt) * 1.0001)
+        # near zero the fp32 dot product cancels: allow its absolute error too
+        assert np.all(np.abs(lg - ref)[d] <= np.maximum(2 * ulp(ref[d], dt) * 1.0001, LOGIT_ABS_TOL))
 
 
 @pytest.mark.parametrize("name", [n for n in NAMES if n != "c2_bf16"])
