@@ -95,6 +95,12 @@ typedef struct SagaAttnArgs {
 
   void* workspace; size_t workspace_bytes; /* see saga_workspace_bytes */
   int32_t* status; /* device status word (SAGA_STATUS_*), or NULL */
+
+  /* Optional phase trace (NULL = off): CTA c < 1024 writes SM clock stamps
+   * (clock64) of its first work item at trace[c * 16 + k], k = 0 start,
+   * 1 logits done, 2..6 after each inter-CTA exchange or the value gather,
+   * 7 item done. Diagnostics only. */
+  int64_t* trace;
 } SagaAttnArgs;
 
 /* Ops understood by saga_workspace_bytes. */

@@ -40,6 +40,7 @@ class SagaAttnArgs(ctypes.Structure):
         ("logits_out", _vp), ("lo_ld", _i64),
         ("workspace", _vp), ("workspace_bytes", _sz),
         ("status", _vp),
+        ("trace", _vp),
     ]
 
 

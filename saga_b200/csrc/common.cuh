@@ -208,13 +208,18 @@ __device__ __forceinline__ bool group_barrier(int* ctr, int target, bool arrive,
     if (arrive) atomicAdd(ctr, 1);
     int ok = 1;
     if (ld_acquire_gpu(ctr) < target) {
-      const unsigned long long t0 = globaltimer_ns();
-      while (ld_acquire_gpu(ctr) < target) {
-        __nanosleep(40);
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-          ok = 0;
-          if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
-          break;
+      // poll the counter; read the clock only every 256 polls
+      unsigned long long t0 = 0;
+      for (uint32_t i = 1; ld_acquire_gpu(ctr) < target; ++i) {
+        if ((i & 255u) == 0) {
+          const unsigned long long now = globaltimer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kWaitLimitNs) {
+            ok = 0;
+            if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
+            break;
+          }
         }
       }
     }

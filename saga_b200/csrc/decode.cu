@@ -2,8 +2,7 @@
 //
 // Work item = (group g = batch x key head, chunk j of the sequence). The C
 // chunks of a group run concurrently (cooperative launch, static round-robin
-// assignment) and exchange per-chunk statistics through the workspace with
-// bounded group barriers. Per item:
+// assignment). Per item:
 //   score   the G query heads of the group against the chunk's keys. For
 //           bf16/fp16: TMA streams 128-position K tiles (128-B swizzle) through
 //           a ring of shared-memory stages; one thread issues tcgen05 UMMAs
@@ -13,19 +12,25 @@
 //           is applied (GEMM -> dtype, * scaling -> dtype, + mask -> dtype;
 //           attention.py:113-128) and the logits stay in shared memory;
 //   then, by mode:
-//   amortized (attention.py:192-209): tail max over the last 256 logits,
-//           partial exp-sums, logit threshold (136-149), strict selection and
-//           per-chunk counts (triton_atopn.py:42), exclusive prefix of counts
-//           so that at most K = min(2N, L) lowest positions are kept, softmax
-//           weights exp(l - m_chunk) over the kept logits;
+//   amortized (attention.py:192-209): every CTA first scores the last 256
+//           positions itself, so the tail max m (attention.py:142-143) needs
+//           no exchange, and the exp-sum of its chunk (145) is accumulated by
+//           the scoring epilogue; one exchange of the partial sums gives the
+//           logit threshold (147); strict selection (triton_atopn.py:42); one
+//           exchange of the per-chunk counts keeps the K = min(2N, L) lowest
+//           passing positions; softmax weights exp(l - m_chunk);
 //   calibrate (attention.py:173-189): global max and sum of exp, exact N-th
 //           largest logit by an 8-bit-per-pass radix select over the group,
 //           its probability as the threshold, top-N set (ties by position),
 //           weights = the dtype-rounded probabilities;
 //   dense   (attention.py:64-85): weights exp(l - m_chunk) for all positions;
-//   then the V gather: every needed value row is fetched once per value head
-//   with bulk copies into shared memory, weighted in fp32 per query head, and
-//   written as a partial (m, l, o[D]); the group's chunks merge the partials.
+//   then the V gather (every needed value row fetched once per value head),
+//   a partial (m, l, o[D]) per head, and a merge split across the chunks.
+//
+// Exchanges between the chunks of a group go through epoch-tagged 64-bit
+// slots (32-bit launch tag | 32-bit value): a reader polls the data itself,
+// one L2 round trip when it is ready, with no separate counter. The group's
+// last chunk to finish advances the epoch for the next launch.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -47,9 +52,12 @@ struct Misc {
   uint64_t empty[kMaxStages];  // K stage free again (UMMA commit)
   uint64_t tfull[2];           // TMEM accumulator ready (UMMA commit)
   uint64_t tempty[2];          // TMEM accumulator drained (4 epilogue warps)
-  uint64_t vbar;               // value rows landed (bulk copies)
+  uint64_t tdone;              // tail tiles scored by the 4 epilogue warps
   uint32_t tmem_slot;
   int abort;
+  uint32_t tag;        // exchange tag of this launch for the current group
+  uint32_t tkey[kMaxG];        // order-preserving keys of the tail max
+  float ered[4][kMaxG];        // per-epilogue-warp partial exp-sums / maxima
   float m[kMaxG];      // tail max / global max
   float t[kMaxG];      // logit threshold / N-th logit
   float s[kMaxG];      // exp-sum
@@ -66,7 +74,7 @@ struct Misc {
   int flag;
   int last;
 };
-static_assert(sizeof(Misc) <= 2048, "Misc must fit its 2 KB slot");
+static_assert(sizeof(Misc) <= 4096, "Misc must fit its 4 KB slot");
 
 // Per-thread pipeline positions kept across items (only role threads use theirs).
 struct Ring {
@@ -74,7 +82,7 @@ struct Ring {
   uint32_t ms = 0, mph = 0;   // UMMA issuer stage / phase
   uint32_t mb = 0, mbph = 0;  // UMMA issuer TMEM buffer / phase
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
-  uint32_t vph = 0;           // value-row barrier phase (all threads)
+  uint32_t tph = 0;           // tail-done barrier phase (epilogue warps)
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -86,6 +94,66 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Order-preserving unsigned key of any float (NaN with a positive sign bit
+// sorts above +inf, so a max over keys propagates it as torch.max does).
+__device__ __forceinline__ uint32_t fkey(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float funkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// ---------------------------------------------------------------------------
+// Epoch-tagged exchange slots
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void slot_put(unsigned long long* p, uint32_t tag, uint32_t bits) {
+  const unsigned long long v = ((unsigned long long)tag << 32) | bits;
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until the slot carries `tag`; returns its 32-bit value (bounded wait).
+__device__ __forceinline__ uint32_t slot_wait(const unsigned long long* p, unsigned long long v, uint32_t tag,
+                                              int* status) {
+  if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+  unsigned long long t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    v = slot_ld(p);
+    if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
+    if ((i & 255u) == 0) {
+      const unsigned long long now = globaltimer_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
+        return (uint32_t)v;
+      }
+    }
+  }
+}
+// All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i],
+// issuing 8 independent loads per thread before waiting on any of them.
+template <typename AddrFn>
+__device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t tag, uint32_t* dst, int* status) {
+  for (int base = threadIdx.x; base < count; base += kThreads * 8) {
+    unsigned long long v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + k * kThreads;
+      v[k] = (i < count) ? slot_ld(addr(i)) : 0ull;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + k * kThreads;
+      if (i < count) dst[i] = slot_wait(addr(i), v[k], tag, status);
+    }
+  }
 }
 
 // The reference's rounding chain for one logit (attention.py:121-126).
@@ -100,29 +168,42 @@ __device__ __forceinline__ float finalize_logit(const DecodeParams& p, float acc
   return l;
 }
 
+// One term of the reference's exp-sum: exp(l - m) with both steps rounded to
+// the dtype (attention.py:145). The fast exp differs from an accurate one by a
+// few fp32 ulps, which the rounding to bf16/fp16 absorbs except at rounding
+// boundaries; fp32 uses the accurate expf.
+template <typename T>
+__device__ __forceinline__ float exp_term(float l, float m) {
+  const float d = Num<T>::round(__fsub_rn(l, m));
+  return Num<T>::round(Num<T>::kLowp ? __expf(d) : expf(d));
+}
+
 // ---------------------------------------------------------------------------
 // Scoring on CUDA cores (fp32 path). 64-position sub-tiles of K are staged in
 // SMEM with cp.async (rows padded by 16 B); thread t scores position t % 64
-// for the heads of slice t / 64.
+// for the heads of slice t / 64. Positions [a, a + cnt) are scored; with
+// max_only they only raise misc->tkey (the tail max), else they are stored at
+// sc[hl * CL + (pos - p0)].
 // ---------------------------------------------------------------------------
 template <typename T, int D>
-__device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, int n,
-                                 const float* __restrict__ qf, T* __restrict__ sc, uint8_t* __restrict__ stage) {
+__device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, int cnt, int p0, bool max_only,
+                                 const float* __restrict__ qf, T* __restrict__ sc, uint8_t* __restrict__ stage,
+                                 Misc* misc) {
   constexpr int SUB = 64;
   constexpr int ROWB = D * (int)sizeof(T);
   constexpr int PITCH = ROWB + 16;
   constexpr int CPR = ROWB / 16;
   const int CL = p.CL;
   const T* kbase = reinterpret_cast<const T*>(p.k) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh;
-  const int nsub = (n + SUB - 1) / SUB;
+  const int nsub = (cnt + SUB - 1) / SUB;
   const int h0 = kh * p.G;
 
   auto issue = [&](int s) {
     uint8_t* buf = stage + (s & 1) * SUB * PITCH;
     for (int c = threadIdx.x; c < SUB * CPR; c += kThreads) {
       const int r = c / CPR, cc = c % CPR;
-      const bool ok = (s * SUB + r) < n;
-      const T* src = kbase + (int64_t)(ok ? (p0 + s * SUB + r) : p0) * p.k_sl + cc * (16 / (int)sizeof(T));
+      const bool ok = (s * SUB + r) < cnt;
+      const T* src = kbase + (int64_t)(ok ? (a + s * SUB + r) : a) * p.k_sl + cc * (16 / (int)sizeof(T));
       cp_async16(buf + r * PITCH + cc * 16, src, ok);
     }
     cp_async_commit();
@@ -157,21 +238,26 @@ __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, i
           const float* qr = qf + (hbeg + hh) * D + d;
           const float4 qa = *reinterpret_cast<const float4*>(qr);
           const float4 qb = *reinterpret_cast<const float4*>(qr + 4);
-          float a = acc[hh];
-          a = fmaf(kf[0], qa.x, a); a = fmaf(kf[1], qa.y, a);
-          a = fmaf(kf[2], qa.z, a); a = fmaf(kf[3], qa.w, a);
-          a = fmaf(kf[4], qb.x, a); a = fmaf(kf[5], qb.y, a);
-          a = fmaf(kf[6], qb.z, a); a = fmaf(kf[7], qb.w, a);
-          acc[hh] = a;
+          float x = acc[hh];
+          x = fmaf(kf[0], qa.x, x); x = fmaf(kf[1], qa.y, x);
+          x = fmaf(kf[2], qa.z, x); x = fmaf(kf[3], qa.w, x);
+          x = fmaf(kf[4], qb.x, x); x = fmaf(kf[5], qb.y, x);
+          x = fmaf(kf[6], qb.z, x); x = fmaf(kf[7], qb.w, x);
+          acc[hh] = x;
         }
       }
     }
-    const int pl = s * SUB + pos_l;
-    if (pl < n) {
+    const int pr = s * SUB + pos_l;
+    if (pr < cnt) {
+      const int pos = a + pr;
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh) {
         const int hl = hbeg + hh;
-        if (hl < hend) sc[hl * CL + pl] = Num<T>::from_f(finalize_logit<T>(p, acc[hh], b, h0 + hl, p0 + pl));
+        if (hl < hend) {
+          const float l = finalize_logit<T>(p, acc[hh], b, h0 + hl, pos);
+          if (max_only) atomicMax(&misc->tkey[hl], fkey(l));
+          else sc[hl * CL + (pos - p0)] = Num<T>::from_f(l);
+        }
       }
     }
     __syncthreads();
@@ -183,13 +269,17 @@ __device__ void score_chunk_simt(const DecodeParams& p, int b, int kh, int p0, i
 //   warp 0 lane 0: TMA producer of 128 x D key tiles (ring of ns stages);
 //   warp 1 lane 0: UMMA issuer, D(128 x 16, fp32 in TMEM) = K_tile . Q^T;
 //   warps 4-7    : epilogue, lane = position, 16 columns = query-head slots.
+// The tile sequence is n_pre tail tiles (global tile indices pre0 ...), whose
+// logits only raise the tail max, then the chunk's own tiles. With the tail
+// max known, the epilogue accumulates the chunk's exp-sum (amortized) or its
+// maximum (other modes) per head into misc->ered.
 // The query operand (16 rows, zero padded beyond G) is written into SMEM in the
 // same 128-B swizzled K-major layout the TMA produces for the key tiles.
 // ---------------------------------------------------------------------------
-template <typename T, int D>
-__device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int n, T* __restrict__ sc,
-                               uint8_t* __restrict__ qop, uint8_t* __restrict__ ring, Misc* misc, Ring& rg,
-                               uint32_t tmem_base) {
+template <typename T, int D, int MODE>
+__device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int n, int pre0, int n_pre,
+                               T* __restrict__ sc, uint8_t* __restrict__ qop, uint8_t* __restrict__ ring,
+                               Misc* misc, Ring& rg, uint32_t tmem_base) {
   constexpr int KB = D / 64;  // 128-byte K blocks per row
   constexpr uint32_t TILE_BYTES = 128u * D * 2u;
   constexpr uint32_t IDESC = umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16);
@@ -197,6 +287,8 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
   const int G = p.G, CL = p.CL, NS = p.ns;
   const int h0 = kh * G;
   const int ntl = (n + 127) / 128;
+  const int nseq = n_pre + ntl;
+  const int tail_start = p.L - p.tail;
 
   // B operand: query heads of the group as 16 rows x D, swizzled.
   for (int i = threadIdx.x; i < 16 * (D / 8); i += kThreads) {
@@ -208,22 +300,24 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     for (int e = 0; e < 8; ++e) vals[e] = (h < G) ? src[e] : Num<T>::from_f(0.f);
     *reinterpret_cast<uint4*>(qop + kb * 2048 + h * 128 + ((c ^ (h & 7)) << 4)) = *reinterpret_cast<uint4*>(vals);
   }
+  for (int hl = threadIdx.x; hl < kMaxG; hl += kThreads) misc->tkey[hl] = 0u;
   fence_proxy_async_smem();
   __syncthreads();
 
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      for (int t = 0; t < ntl && !misc->abort; ++t) {
+      for (int q = 0; q < nseq && !misc->abort; ++q) {
         if (!mbar_wait(&misc->empty[rg.ps], rg.pph ^ 1u, p.status)) {
           misc->abort = 1;
           break;
         }
+        const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
         mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
         uint8_t* dst = ring + rg.ps * TILE_BYTES;
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb)
-          tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, p0 + t * 128, kh, b, &misc->full[rg.ps]);
+          tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
         ++issued;
         if (++rg.ps == (uint32_t)NS) {
           rg.ps = 0;
@@ -248,7 +342,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     if (lane == 0) {
       int issued = 0;
       uint32_t last_b = 0, last_ph = 0;
-      for (int t = 0; t < ntl && !misc->abort; ++t) {
+      for (int q = 0; q < nseq && !misc->abort; ++q) {
         if (!mbar_wait(&misc->full[rg.ms], rg.mph, p.status) ||
             !mbar_wait(&misc->tempty[rg.mb], rg.mbph ^ 1u, p.status)) {
           misc->abort = 1;
@@ -283,8 +377,15 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     }
   } else if (warp >= 4) {
     const int q4 = warp - 4;  // TMEM lane quarter of this warp
-    for (int t = 0; t < ntl; ++t) {
-      bool ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
+    float m[16], acc[16];
+#pragma unroll
+    for (int hl = 0; hl < 16; ++hl) {
+      m[hl] = 0.f;
+      acc[hl] = (MODE == MODE_AMORTIZED) ? 0.f : -INFINITY;
+    }
+    bool ok = true;
+    for (int q = 0; q < nseq; ++q) {
+      ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         if (lane == 0) misc->abort = 1;
@@ -300,12 +401,47 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         rg.eb = 0;
         rg.ebph ^= 1u;
       }
-      const int pl = t * 128 + q4 * 32 + lane;
+      if (q < n_pre) {
+        // tail tile: raise the tail max of each head
+        const int pos = (pre0 + q) * 128 + q4 * 32 + lane;
+        const bool in_tail = pos >= tail_start && pos < p.L;
+#pragma unroll
+        for (int hl = 0; hl < 16; ++hl) {
+          if (hl < G) {
+            float l = in_tail ? finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, pos) : -INFINITY;
+            l = warp_nanmax(l);
+            if (lane == 0) atomicMax(&misc->tkey[hl], fkey(l));
+          }
+        }
+        if (q == n_pre - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&misc->tdone);
+          mbar_wait(&misc->tdone, rg.tph, p.status);
+          rg.tph ^= 1u;
+#pragma unroll
+          for (int hl = 0; hl < 16; ++hl) m[hl] = (hl < G) ? funkey(misc->tkey[hl]) : 0.f;
+        }
+        continue;
+      }
+      const int pl = (q - n_pre) * 128 + q4 * 32 + lane;
       if (pl < n) {
 #pragma unroll
-        for (int hl = 0; hl < 16; ++hl)
-          if (hl < G)
-            sc[hl * CL + pl] = Num<T>::from_f(finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, p0 + pl));
+        for (int hl = 0; hl < 16; ++hl) {
+          if (hl < G) {
+            const float l = finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, p0 + pl);
+            sc[hl * CL + pl] = Num<T>::from_f(l);
+            if constexpr (MODE == MODE_AMORTIZED) acc[hl] += exp_term<T>(l, m[hl]);
+            else acc[hl] = nanmax(acc[hl], l);
+          }
+        }
+      }
+    }
+    // per-warp partials of the exp-sum / maximum (reduced in fixed order later)
+#pragma unroll
+    for (int hl = 0; hl < 16; ++hl) {
+      if (hl < G) {
+        const float v = (MODE == MODE_AMORTIZED) ? warp_sum(acc[hl]) : warp_nanmax(acc[hl]);
+        if (lane == 0) misc->ered[q4][hl] = v;
       }
     }
   }
@@ -374,29 +510,36 @@ __device__ __forceinline__ float weight_of(const T* sc, int CL, const Misc* misc
   if constexpr (MODE == MODE_CALIBRATE)
     return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, misc->m[hl])), misc->s[hl]));
   else
-    return expf(l - misc->aux[hl]);
+    return __expf(l - misc->aux[hl]);
 }
+
+// Slot address: group g, chunk c, local head hl, field k.
+__device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k) {
+  return p.slots + (((size_t)g * p.C + c) * p.G + hl) * (size_t)(p.D + 4) + k;
+}
+constexpr int kSlotS = 0, kSlotCnt = 1, kSlotM = 2, kSlotL = 3, kSlotO = 4;
 
 // ---------------------------------------------------------------------------
 // V gather of one item. For each value head of the group and each batch of up
 // to 8 of its query heads, the positions any of them selected form a list;
-// their value rows are fetched once with bulk copies (one lane per row) into
-// SMEM, weighted per query head and accumulated in fp32 per warp, then
-// reduced across warps in a fixed order into the partial o[D]; l = sum of the
-// weights; m = the stabiliser.
+// their value rows are fetched once (cp.async, 16 B per thread and request)
+// into SMEM, weighted per query head and accumulated in fp32 per warp, then
+// reduced across warps in a fixed order. The partial (m, l, o[D]) of every
+// head is published through the group's tagged slots.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int MODE>
-__device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n, const T* __restrict__ sc,
-                            const uint32_t* __restrict__ sel, uint32_t* __restrict__ list, uint8_t* __restrict__ work,
-                            float* __restrict__ wbuf, float* __restrict__ part, Misc* misc, Ring& rg) {
+__device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, int p0, int n,
+                            const T* __restrict__ sc, const uint32_t* __restrict__ sel, uint32_t* __restrict__ list,
+                            uint8_t* __restrict__ work, float* __restrict__ wbuf, Misc* misc) {
   constexpr int EPL = D / 32;
-  constexpr int PS = D + 4;
-  constexpr uint32_t ROWB = D * sizeof(T);
+  constexpr int ROWB = D * (int)sizeof(T);
+  constexpr int CPR = ROWB / 16;
   constexpr bool kDense = (MODE == MODE_DENSE);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, Gv = p.Gv, CL = p.CL, nw = (n + 31) / 32;
   const int BR = p.sm.br;
   const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
+  const uint32_t tag = misc->tag;
 
   // l = sum of the weights per head (fixed order)
   for (int hl = warp; hl < G; hl += kWarps) {
@@ -458,8 +601,9 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
     const int g0 = misc->gstart[gi], g1 = misc->gstart[gi + 1];
     const int vh = misc->gvh[gi];
     const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
-    const T* vrow0 =
-        reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh + (int64_t)p0 * p.v_sl;
+    const uint8_t* vrow0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb +
+                                                           (int64_t)vh * p.v_sh + (int64_t)p0 * p.v_sl);
+    const int64_t vstride = p.v_sl * (int64_t)sizeof(T);
     float acc[8][EPL];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
@@ -468,14 +612,12 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
 
     for (int e0 = g0; e0 < g1; e0 += BR) {
       const int rows = min(BR, g1 - e0);
-      if (warp == 0) {
-        if (lane == 0) mbar_arrive_expect_tx(&misc->vbar, (uint32_t)rows * ROWB);
-        __syncwarp();
-        for (int r = lane; r < rows; r += 32) {
-          const int pos = list[e0 + r] & 0xFFFF;
-          bulk_load(work + (size_t)r * ROWB, vrow0 + (int64_t)pos * p.v_sl, ROWB, &misc->vbar);
-        }
+      for (int i = threadIdx.x; i < rows * CPR; i += kThreads) {
+        const int r = i / CPR, c = i % CPR;
+        const int pos = list[e0 + r] & 0xFFFF;
+        cp_async16(work + (size_t)r * ROWB + c * 16, vrow0 + (int64_t)pos * vstride + c * 16, true);
       }
+      cp_async_commit();
       // weights of the batch while the rows land
       for (int i = threadIdx.x; i < rows * 8; i += kThreads) {
         const int r = i >> 3, hh = i & 7;
@@ -484,8 +626,7 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
         if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, CL, misc, hb + hh, ent & 0xFFFF);
         wbuf[i] = wv;
       }
-      mbar_wait(&misc->vbar, rg.vph, p.status);
-      rg.vph ^= 1u;
+      cp_async_wait<0>();
       __syncthreads();
       for (int r = warp; r < rows; r += kWarps) {
         float vf[EPL];
@@ -512,23 +653,23 @@ __device__ void gather_item(const DecodeParams& p, int b, int h0, int p0, int n,
       float s = 0.f;
 #pragma unroll
       for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
-      part[(hb + hh) * PS + 4 + d] = s;
+      slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(s));
     }
     __syncthreads();
   }
   for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-    part[hl * PS + 0] = (MODE == MODE_CALIBRATE) ? 0.f : misc->aux[hl];
-    part[hl * PS + 1] = misc->lsum[hl];
+    slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
+    slot_put(slot_at(p, g, j, hl, kSlotL), tag, __float_as_uint(misc->lsum[hl]));
   }
 }
 
 // ---------------------------------------------------------------------------
 // Merge of the group's partials: chunk j produces outputs [lo, hi) of the
-// flattened (local head, d) space. Fixed-order sums.
+// flattened (local head, d) space. All the partials it needs are fetched in
+// one burst; sums run in chunk order.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int MODE>
-__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, float* scratch, Misc* misc) {
-  constexpr int PS = D + 4;
+__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, uint8_t* scratch, Misc* misc) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, C = p.C;
   const int tot = G * D;
@@ -537,45 +678,48 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
   if (lo >= hi) return;
   const int hl0 = lo / D, hl1 = (hi - 1) / D;
   const int nhs = hl1 - hl0 + 1;
-  const float* pg = p.partials + (size_t)g * C * G * PS;
-  float* scl = scratch;  // [nhs][C]
+  const int nout = hi - lo;
+  const uint32_t tag = misc->tag;
+  uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][C][2]
+  uint32_t* ov = ml + nhs * C * 2;                      // [nout][C]
+  const int n_ml = nhs * C * 2;
+  slots_gather(
+      n_ml + nout * C,
+      [&](int i) {
+        if (i < n_ml) {
+          const int hh = i / (2 * C), r = i % (2 * C);
+          return slot_at(p, g, r >> 1, hl0 + hh, kSlotM + (r & 1));
+        }
+        const int k = i - n_ml;
+        const int o = lo + k / C, c = k % C;
+        return slot_at(p, g, c, o / D, kSlotO + o % D);
+      },
+      tag, ml, p.status);
+  __syncthreads();
+  float* scl = reinterpret_cast<float*>(ov + nout * C);  // [nhs][C]
   for (int hh = warp; hh < nhs; hh += kWarps) {
-    const int hl = hl0 + hh;
     float M = -INFINITY;
-    for (int c = lane; c < C; c += 32) M = nanmax(M, __ldcg(&pg[((size_t)c * G + hl) * PS + 0]));
+    for (int c = lane; c < C; c += 32) M = nanmax(M, __uint_as_float(ml[(hh * C + c) * 2]));
     M = warp_nanmax(M);
     float Ls = 0.f;
     for (int c = lane; c < C; c += 32) {
-      const float mc = __ldcg(&pg[((size_t)c * G + hl) * PS + 0]);
-      const float f = (MODE == MODE_CALIBRATE) ? 1.f : expf(mc - M);
+      const float mc = __uint_as_float(ml[(hh * C + c) * 2]);
+      const float f = (MODE == MODE_CALIBRATE) ? 1.f : __expf(mc - M);
       scl[hh * C + c] = f;
-      Ls += __ldcg(&pg[((size_t)c * G + hl) * PS + 1]) * f;
+      Ls += __uint_as_float(ml[(hh * C + c) * 2 + 1]) * f;
     }
     Ls = warp_sum(Ls);
     // calibration renormalises by max(sum p, 1e-12) (attention.py:161)
     if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(Ls, 1e-12f) : Ls;
   }
   __syncthreads();
-  int lpo = 1;
-  while (lpo < C && lpo < 32) lpo <<= 1;
-  const int opw = 32 / lpo;
-  const int sub = lane / lpo, sl = lane % lpo;
-  for (int o0 = lo + warp * opw; o0 < hi; o0 += kWarps * opw) {
-    const int o = o0 + sub;
+  for (int k = threadIdx.x; k < nout; k += kThreads) {
+    const int o = lo + k;
+    const int hh = o / D - hl0, d = o % D;
     float acc = 0.f;
-    int hl = 0, d = 0;
-    if (o < hi) {
-      hl = o / D;
-      d = o % D;
-      const int hh = hl - hl0;
-      for (int c = sl; c < C; c += lpo) acc += __ldcg(&pg[((size_t)c * G + hl) * PS + 4 + d]) * scl[hh * C + c];
-    }
-    for (int off = lpo >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (o < hi && sl == 0) {
-      const float r = acc / misc->lsum[hl - hl0];
-      T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + hl) * p.o_sh + d;
-      *out = Num<T>::from_f(r);
-    }
+    for (int c = 0; c < C; ++c) acc += __uint_as_float(ov[k * C + c]) * scl[hh * C + c];
+    T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + o / D) * p.o_sh + d;
+    *out = Num<T>::from_f(acc / misc->lsum[hh]);
   }
 }
 
@@ -638,7 +782,6 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, C = p.C, CL = p.CL;
-  constexpr int PS = D + 4;
   Ring rg;
   uint32_t tmem_base = 0;
 
@@ -651,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       mbar_init(&misc->tfull[bb], 1);
       mbar_init(&misc->tempty[bb], 4);
     }
-    mbar_init(&misc->vbar, 1);
+    mbar_init(&misc->tdone, 4);
     misc->abort = 0;
     mbar_fence_init();
   }
@@ -672,18 +815,26 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     const int n = min(p.L - p0, CL);
     const int nw = (n + 31) / 32;
     int* ctrl = p.ctrl + (size_t)g * kCtrlInts;
-    ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G]
+    ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G] (calibration)
     ChunkStat* st = stg + (size_t)j * G;
     const int row0 = b * p.Hq + h0;
+    const bool tracing = p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
+#define SAGA_TRACE(k) \
+  if (tracing) p.trace[blockIdx.x * 16 + (k)] = clock64();
+    SAGA_TRACE(0)
+    if (threadIdx.x == 0) misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
 
-    // ---- fused append of the decode token (StaticLayer.update's index_copy_)
-    if (p.k_new && p.append_pos >= p0 && p.append_pos < p0 + n) {
+    // ---- fused append of the decode token (StaticLayer.update's index_copy_).
+    // Every chunk of the group writes the new key row (the same values) before
+    // it reads the cache, because every chunk scores the tail positions; the
+    // chunk that owns the position also writes the value rows it gathers.
+    if (p.k_new) {
       const int pos = p.append_pos;
       const T* src = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.kn_sb + (int64_t)kh * p.kn_sh;
       T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh +
                (int64_t)pos * p.k_sl;
       for (int d = threadIdx.x; d < D; d += kThreads) dst[d] = src[d];
-      if (p.v_new) {
+      if (p.v_new && pos >= p0 && pos < p0 + n) {
         const int vh_lo = h0 / p.Gv, vh_hi = (h0 + G - 1) / p.Gv;
         for (int i = threadIdx.x; i < (vh_hi - vh_lo + 1) * D; i += kThreads) {
           const int vh = vh_lo + i / D, d = i % D;
@@ -694,21 +845,60 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         }
       }
       __threadfence_block();
-      fence_proxy_async_global();  // the appended rows are read back by TMA / bulk copies
+      fence_proxy_async_global();  // the appended rows are read back by TMA
     }
 
-    // ---- logits of the chunk
+    // ---- logits of the chunk (and, for amortized, the tail max first)
+    const int tail_start = p.L - p.tail;
     if constexpr (TC) {
+      int pre0 = 0, n_pre = 0;
+      if (MODE == MODE_AMORTIZED) {
+        pre0 = tail_start / kTile;
+        n_pre = (p.L + kTile - 1) / kTile - pre0;
+      }
       __syncthreads();
-      score_chunk_tc<T, D>(p, b, kh, p0, n, sc, qop, work, misc, rg, tmem_base);
+      score_chunk_tc<T, D, MODE>(p, b, kh, p0, n, pre0, n_pre, sc, qop, work, misc, rg, tmem_base);
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        if (MODE == MODE_AMORTIZED) {
+          misc->m[hl] = funkey(misc->tkey[hl]);
+          misc->s[hl] = ((misc->ered[0][hl] + misc->ered[1][hl]) + misc->ered[2][hl]) + misc->ered[3][hl];
+        } else {
+          misc->aux[hl] = nanmax(nanmax(misc->ered[0][hl], misc->ered[1][hl]), nanmax(misc->ered[2][hl], misc->ered[3][hl]));
+        }
+      }
+      __syncthreads();
     } else {
       for (int i = threadIdx.x; i < G * D; i += kThreads) {
         const int hl = i / D, d = i % D;
         qf[i] = Num<T>::to_f(reinterpret_cast<const T*>(p.q)[(int64_t)b * p.q_sb + (int64_t)(h0 + hl) * p.q_sh + d]);
       }
+      for (int hl = threadIdx.x; hl < kMaxG; hl += kThreads) misc->tkey[hl] = 0u;
       __syncthreads();
-      score_chunk_simt<T, D>(p, b, kh, p0, n, qf, sc, work);
+      if (MODE == MODE_AMORTIZED)
+        score_range_simt<T, D>(p, b, kh, tail_start, p.tail, p0, true, qf, sc, work, misc);
+      score_range_simt<T, D>(p, b, kh, p0, n, p0, false, qf, sc, work, misc);
+      for (int hl = warp; hl < G; hl += kWarps) {
+        const float m = funkey(misc->tkey[hl]);
+        float s = 0.f, mx = -INFINITY;
+        for (int i = lane; i < n; i += 32) {
+          const float l = Num<T>::to_f(sc[hl * CL + i]);
+          if (MODE == MODE_AMORTIZED) s += exp_term<T>(l, m);
+          else mx = nanmax(mx, l);
+        }
+        s = warp_sum(s);
+        mx = warp_nanmax(mx);
+        if (lane == 0) {
+          if (MODE == MODE_AMORTIZED) {
+            misc->m[hl] = m;
+            misc->s[hl] = s;
+          } else {
+            misc->aux[hl] = mx;
+          }
+        }
+      }
+      __syncthreads();
     }
+    SAGA_TRACE(1)
 
     if constexpr (MODE == MODE_LOGITS) {
       T* lo = reinterpret_cast<T*>(p.logits_out);
@@ -720,45 +910,24 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       continue;
     }
 
+    const uint32_t tag = misc->tag;
+    uint32_t* xbuf = reinterpret_cast<uint32_t*>(work);  // exchange staging [C][G]
+
     if constexpr (MODE == MODE_AMORTIZED) {
-      const int tail_start = p.L - p.tail;
-      // the chunk's part of the tail max (attention.py:142-143)
-      for (int hl = warp; hl < G; hl += kWarps) {
-        float tm = -INFINITY;
-        for (int i = lane; i < n; i += 32)
-          if (p0 + i >= tail_start) tm = nanmax(tm, Num<T>::to_f(sc[hl * CL + i]));
-        tm = warp_nanmax(tm);
-        if (lane == 0) st[hl].tmx = tm;
-      }
-      const int first_tail = tail_start / CL;
-      const bool is_tail = (p0 + n > tail_start);
-      group_barrier(&ctrl[0], C - first_tail, is_tail, p.status, &misc->flag);
-      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-        float m = -INFINITY;
-        for (int c = first_tail; c < C; ++c) m = nanmax(m, __ldcg(&stg[(size_t)c * G + hl].tmx));
-        misc->m[hl] = m;
-      }
+      // exchange the partial exp-sums (attention.py:145: sum over the row)
+      for (int hl = threadIdx.x; hl < G; hl += kThreads)
+        slot_put(slot_at(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
+      slots_gather(C * G, [&](int i) { return slot_at(p, g, i / G, i % G, kSlotS); }, tag, xbuf, p.status);
       __syncthreads();
-      // partial s = sum(exp(logits - m)), each step rounded as the reference
-      // does in the dtype (attention.py:145)
-      for (int hl = warp; hl < G; hl += kWarps) {
-        const float m = misc->m[hl];
-        float s = 0.f;
-        for (int i = lane; i < n; i += 32)
-          s += Num<T>::round(expf(Num<T>::round(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), m))));
-        s = warp_sum(s);
-        if (lane == 0) st[hl].s = s;
-      }
-      group_barrier(&ctrl[1], C, true, p.status, &misc->flag);
+      SAGA_TRACE(2)
       // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         float s = 0.f;
-        for (int c = 0; c < C; ++c) s += __ldcg(&stg[(size_t)c * G + hl].s);
+        for (int c = 0; c < C; ++c) s += __uint_as_float(xbuf[c * G + hl]);
         s = Num<T>::round(s);
         const float thr = clamp_min_keep_nan(p.thr_in[row0 + hl], 1e-30f);
         const float t = __fadd_rn(misc->m[hl], logf(__fmul_rn(thr, s)));
         misc->t[hl] = t;
-        misc->s[hl] = s;
         if (j == 0) {
           if (p.logit_thr_out) p.logit_thr_out[row0 + hl] = t;
           if (!isfinite(t)) set_status(p.status, SAGA_STATUS_NONFINITE_THR);
@@ -777,21 +946,25 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
           cnt += __popc(bits);
         }
         if (lane == 0) {
-          st[hl].cnt = cnt;
           misc->i2[hl] = cnt;
+          slot_put(slot_at(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
         }
       }
-      group_barrier(&ctrl[2], C, true, p.status, &misc->flag);
+      __syncthreads();
+      SAGA_TRACE(3)
+      slots_gather(C * G, [&](int i) { return slot_at(p, g, i / G, i % G, kSlotCnt); }, tag, xbuf, p.status);
+      __syncthreads();
+      SAGA_TRACE(4)
       // exclusive prefix in chunk order: keep the K lowest passing positions
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         int pre = 0, tot = 0;
         for (int c = 0; c < C; ++c) {
-          const int cc = __ldcg(&stg[(size_t)c * G + hl].cnt);
+          const int cc = (int)xbuf[c * G + hl];
           if (c < j) pre += cc;
           tot += cc;
         }
         const int mine = misc->i2[hl];
-        pre = max(0, pre);  // bounds every offset below even if the stats were corrupt
+        pre = max(0, pre);  // bounds every offset below even if the slots were corrupt
         misc->i0[hl] = pre;
         misc->i1[hl] = max(0, min(mine, p.buf_k - pre));
         if (j == 0) {
@@ -815,26 +988,20 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         if (lane == 0) misc->aux[hl] = m;
       }
       __syncthreads();
-      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, sel, list, work, wbuf,
-                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
-      group_barrier(&ctrl[3], C, true, p.status, &misc->flag);
+      gather_item<T, D, MODE>(p, g, j, b, h0, p0, n, sc, sel, list, work, wbuf, misc);
+      SAGA_TRACE(5)
     } else if constexpr (MODE == MODE_CALIBRATE) {
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
       const int nsel = p.buf_k;  // min(N, L)
       int* hsm = reinterpret_cast<int*>(work);     // [G][256]
       int* gh = p.hist + (size_t)g * 4 * G * 256;  // [pass][G][256]
-      for (int hl = warp; hl < G; hl += kWarps) {
-        float mx = -INFINITY;
-        for (int i = lane; i < n; i += 32) mx = nanmax(mx, Num<T>::to_f(sc[hl * CL + i]));
-        mx = warp_nanmax(mx);
-        if (lane == 0) st[hl].mx = mx;
-      }
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        st[hl].mx = misc->aux[hl];
         misc->i0[hl] = nsel;  // rank wanted within the current key prefix
         misc->i1[hl] = 0;     // key prefix so far
       }
-      int sync_id = 1;
+      int sync_id = 2;
       for (int pass = 0; pass < PASSES; ++pass) {
         const int shift = KB - 8 * (pass + 1);
         for (int i = threadIdx.x; i < G * 256; i += kThreads) hsm[i] = 0;
@@ -942,34 +1109,31 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
                                max(0, p.sel_ld - misc->i3[hl]));
       }
       __syncthreads();
-      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, sel, list, work, wbuf,
-                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
-      group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
-    } else {  // MODE_DENSE
-      for (int hl = warp; hl < G; hl += kWarps) {
-        float mx = -INFINITY;
-        for (int i = lane; i < n; i += 32) mx = nanmax(mx, Num<T>::to_f(sc[hl * CL + i]));
-        mx = warp_nanmax(mx);
-        if (lane == 0) misc->aux[hl] = mx;
-      }
-      __syncthreads();
-      gather_item<T, D, MODE>(p, b, h0, p0, n, sc, nullptr, list, work, wbuf,
-                              p.partials + ((size_t)g * C + j) * G * PS, misc, rg);
-      group_barrier(&ctrl[1], C, true, p.status, &misc->flag);
+      gather_item<T, D, MODE>(p, g, j, b, h0, p0, n, sc, sel, list, work, wbuf, misc);
+      SAGA_TRACE(5)
+    } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
+      gather_item<T, D, MODE>(p, g, j, b, h0, p0, n, sc, nullptr, list, work, wbuf, misc);
+      SAGA_TRACE(5)
     }
+    __syncthreads();
 
     // ---- merge of the group's partials, split across its chunks
-    merge_slice<T, D, MODE>(p, g, j, b, h0, reinterpret_cast<float*>(work), misc);
+    merge_slice<T, D, MODE>(p, g, j, b, h0, work, misc);
+    SAGA_TRACE(6)
 
-    // ---- the group's last chunk to finish resets its counters (and histograms)
+    // ---- the group's last chunk to finish advances the epoch and resets
+    // the calibration counters and histograms
     __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      misc->last = (atomicAdd(&ctrl[kCtrlDone], 1) == C - 1);
-    }
+    SAGA_TRACE(7)
+#undef SAGA_TRACE
+    if (threadIdx.x == 0) misc->last = (atomicAdd(&ctrl[kCtrlDone], 1) == C - 1);
     __syncthreads();
     if (misc->last) {
-      for (int i = threadIdx.x; i < kCtrlInts; i += kThreads) ctrl[i] = 0;
+      if (threadIdx.x == 0) {
+        ctrl[kCtrlDone] = 0;
+        ctrl[0] = (int)tag;  // next launch's tag is tag + 1
+      }
+      for (int i = 1 + threadIdx.x; i < kCtrlDone; i += kThreads) ctrl[i] = 0;
       if (MODE == MODE_CALIBRATE) {
         int* gh = p.hist + (size_t)g * 4 * G * 256;
         for (int i = threadIdx.x; i < 4 * G * 256; i += kThreads) gh[i] = 0;
@@ -1094,14 +1258,14 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   const int ntiles = (a->L + kTile - 1) / kTile;
   const int es = esize_of(a->dtype);
   const bool tc = (a->dtype != SAGA_FP32);
-  const int nvh = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
+  const int ngg = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
   // tensor-core path: one CTA per SM, deepest K ring that fits; fp32: two per SM
   const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
   int ns = tc ? kMaxStages : 2, max_tiles = 0;
   for (; ns >= 2; --ns) {
     max_tiles = 0;
     for (int t = 1; t <= ntiles; ++t) {
-      if (smem_layout(G, a->D, t * kTile, es, 4096, tc, ns, nvh).total <= budget) max_tiles = t;
+      if (smem_layout(G, a->D, t * kTile, es, std::min(ntiles, 4096), tc, ns, ngg).total <= budget) max_tiles = t;
       else break;
     }
     if (!tc || max_tiles >= std::min(ntiles, 8)) break;
@@ -1118,7 +1282,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   int tiles = (ntiles + C - 1) / C;
   C = (ntiles + tiles - 1) / tiles;
   const int CL = tiles * kTile;
-  const SmemLayout sm = smem_layout(G, a->D, CL, es, C, tc, ns, nvh);
+  const SmemLayout sm = smem_layout(G, a->D, CL, es, C, tc, ns, ngg);
 
   pl->G = G;
   pl->Gv = Gv;
@@ -1128,7 +1292,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   pl->items = groups * C;
   pl->smem = sm.total;
   pl->ns = ns;
-  pl->nvh = nvh;
+  pl->nvh = ngg;
   pl->tc = tc;
   pl->cooperative = (mode != MODE_LOGITS);
   const void* kfn = pick_kernel(a->dtype, a->D, mode);
@@ -1149,12 +1313,11 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   }
   pl->grid = pl->cooperative ? std::min(pl->items, cap) : pl->items;
 
-  const int PS = a->D + 4;
   pl->ws_ctrl = 0;
   pl->ws_hist = al256((size_t)groups * kCtrlInts * 4);
   pl->ws_stats = pl->ws_hist + (mode == MODE_CALIBRATE ? al256((size_t)groups * 4 * G * 256 * 4) : 0);
-  pl->ws_part = pl->ws_stats + al256((size_t)groups * C * G * sizeof(ChunkStat));
-  pl->ws_total = pl->ws_part + al256((size_t)groups * C * G * PS * 4);
+  pl->ws_part = pl->ws_stats + (mode == MODE_CALIBRATE ? al256((size_t)groups * C * G * sizeof(ChunkStat)) : 0);
+  pl->ws_total = pl->ws_part + al256((size_t)groups * C * G * (a->D + 4) * 8);
   return SAGA_OK;
 }
 
@@ -1193,10 +1356,11 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   if (mode != MODE_LOGITS) {
     p.ctrl = reinterpret_cast<int*>(ws + pl.ws_ctrl);
     p.hist = mode == MODE_CALIBRATE ? reinterpret_cast<int*>(ws + pl.ws_hist) : nullptr;
-    p.stats = reinterpret_cast<ChunkStat*>(ws + pl.ws_stats);
-    p.partials = reinterpret_cast<float*>(ws + pl.ws_part);
+    p.stats = mode == MODE_CALIBRATE ? reinterpret_cast<ChunkStat*>(ws + pl.ws_stats) : nullptr;
+    p.slots = reinterpret_cast<unsigned long long*>(ws + pl.ws_part);
   }
   p.status = a->status;
+  p.trace = reinterpret_cast<long long*>(a->trace);
   p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C, pl.tc, pl.ns, pl.nvh);
 
   if (pl.tc) {

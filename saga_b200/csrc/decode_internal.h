@@ -49,15 +49,20 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   int work = tc ? ns * 128 * rowb : 2 * 64 * (rowb + 16);
   const int red = 8 * 8 * D * 4;
   const int hist = G * 256 * 4;
-  const int merge = (G + 2 * C + 64) * 4 + 256;
+  // merge staging: (m, l) and scale per covered head and chunk, o per output and chunk
+  const int per = (G * D + C - 1) / C;
+  const int nhs = per / D + 2;
+  const int merge = 4 * (nhs * C * 3 + per * C) + 256;
+  const int xchg = 4 * C * G + 256;  // per-chunk exchange staging
   work = work > red ? work : red;
   work = work > hist ? work : hist;
   work = work > merge ? work : merge;
+  work = work > xchg ? work : xchg;
   work = align_up(work, 1024);
   int br = work / rowb;
   br = br > 4096 ? 4096 : br;
   int off = 0;
-  l.misc = off;   off += 2048;
+  l.misc = off;   off += 4096;
   l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
   l.work = off;   off += work;
   l.scores = off; off += align_up(G * CL * esize, 128);
@@ -87,8 +92,10 @@ struct DecodeParams {
   int append_pos;
   float* logit_thr_out; int* count_out; int* sel_idx_out; int sel_ld;
   void* logits_out; int64_t lo_ld;
-  int* ctrl; ChunkStat* stats; float* partials; int* hist;
+  int* ctrl; ChunkStat* stats; int* hist;
+  unsigned long long* slots;  // [group][chunk][head][D + 4] epoch-tagged exchange slots
   int* status;
+  long long* trace;
   SmemLayout sm;
 };
 

@@ -46,15 +46,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait for the phase of `parity` to complete, at most kWaitLimitNs. Returns
 // false (and flags the status word) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  if (mbar_try_wait(bar, parity)) return true;
+  // cheap polls first; the clock is read only every 1024 polls after that
+  for (int i = 0; i < 2048; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
       if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
       return false;
     }
   }
-  return true;
 }
 
 // ---------------------------------------------------------------------------

@@ -162,6 +162,9 @@ def _run(fn_name, a, op, device, diag=None):
     ws = _workspace(a, op, device)
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     a.status = status_tensor(device).data_ptr()
+    if diag is not None and diag.get("trace"):
+        diag["trace"] = torch.zeros((1024, 16), dtype=torch.int64, device=device)
+        a.trace = diag["trace"].data_ptr()
     rc = getattr(L.lib, fn_name)(ctypes.byref(a), _stream(device))
     L.check(rc, fn_name)
     if diag is not None:

@@ -90,7 +90,8 @@ def test_logits(gold, name):
         np.testing.assert_allclose(lg, ref, rtol=1e-5, atol=1e-5)
     else:
         d = lg != ref
-        assert d.mean() < 1e-3
+        # fp16 keeps 3 more mantissa bits than bf16: ~8x more rounding-boundary flips
+        assert d.mean() < (1e-3 if dt == "bf16" else 1e-2)
         # near zero the fp32 dot product cancels: allow its absolute error too
         assert np.all(np.abs(lg - ref)[d] <= np.maximum(2 * ulp(ref[d], dt) * 1.0001, LOGIT_ABS_TOL))
 
