@@ -96,10 +96,11 @@ typedef struct SagaAttnArgs {
   void* workspace; size_t workspace_bytes; /* see saga_workspace_bytes */
   int32_t* status; /* device status word (SAGA_STATUS_*), or NULL */
 
-  /* Optional phase trace (NULL = off): CTA c < 1024 writes SM clock stamps
-   * (clock64) of its first work item at trace[c * 16 + k], k = 0 start,
-   * 1 logits done, 2..6 after each inter-CTA exchange or the value gather,
-   * 7 item done. Diagnostics only. */
+  /* Optional phase trace (NULL = off), int64 [1024][64]: CTA c < 1024 writes
+   * SM clock stamps (clock64) of its first work item at trace[c * 64 + k]:
+   * k = 0 start, 1 logits done, 2..6 after each inter-CTA exchange or the
+   * value gather, 7 item done; 16 + t / 32 + t / 48 + t: key tile t (< 16)
+   * issued by TMA / multiplied / stored by the epilogue. Diagnostics only. */
   int64_t* trace;
 } SagaAttnArgs;
 

@@ -211,6 +211,7 @@ __device__ __forceinline__ bool group_barrier(int* ctr, int target, bool arrive,
       // poll the counter; read the clock only every 256 polls
       unsigned long long t0 = 0;
       for (uint32_t i = 1; ld_acquire_gpu(ctr) < target; ++i) {
+        __nanosleep(32);
         if ((i & 255u) == 0) {
           const unsigned long long now = globaltimer_ns();
           if (t0 == 0) {

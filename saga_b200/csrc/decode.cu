@@ -4,21 +4,24 @@
 // chunks of a group run concurrently (cooperative launch, static round-robin
 // assignment). Per item:
 //   score   the G query heads of the group against the chunk's keys. For
-//           bf16/fp16: TMA streams 128-position K tiles (128-B swizzle) through
-//           a ring of shared-memory stages; one thread issues tcgen05 UMMAs
-//           (M = 128 positions, N = 16 query-head slots, K = D) into a double
-//           buffered TMEM accumulator; four warps read it back (tcgen05.ld).
-//           For fp32: CUDA-core FMAs. Either way the reference rounding chain
-//           is applied (GEMM -> dtype, * scaling -> dtype, + mask -> dtype;
-//           attention.py:113-128) and the logits stay in shared memory;
+//           bf16/fp16 with G <= 16: TMA streams 128-position K tiles (128-B
+//           swizzle) through a ring of shared-memory stages; one thread issues
+//           tcgen05 UMMAs (M = 128 positions, N = 16 query-head slots, K = D)
+//           into a double-buffered TMEM accumulator; four warps read it back
+//           (tcgen05.ld) and finalise head pairs with packed conversions;
+//           two more warps fold each stored tile into the per-head exp-sum /
+//           maximum while the next tiles stream. Otherwise CUDA-core FMAs.
+//           Either way the reference rounding chain is applied (GEMM -> dtype,
+//           * scaling -> dtype, + mask -> dtype; attention.py:113-128) and the
+//           logits stay in shared memory, position-major ([pos][head slot]);
 //   then, by mode:
-//   amortized (attention.py:192-209): every CTA first scores the last 256
-//           positions itself, so the tail max m (attention.py:142-143) needs
-//           no exchange, and the exp-sum of its chunk (145) is accumulated by
-//           the scoring epilogue; one exchange of the partial sums gives the
-//           logit threshold (147); strict selection (triton_atopn.py:42); one
-//           exchange of the per-chunk counts keeps the K = min(2N, L) lowest
-//           passing positions; softmax weights exp(l - m_chunk);
+//   amortized (attention.py:192-209): every CTA scores the last 256 positions
+//           itself, so the tail max m (attention.py:142-143) needs no exchange,
+//           and the exp-sum of its chunk (145) accumulates during scoring; one
+//           exchange of the partial sums gives the logit threshold (147);
+//           strict selection (triton_atopn.py:42); one exchange of per-chunk
+//           counts keeps the K = min(2N, L) lowest passing positions; softmax
+//           weights exp(l - stabiliser);
 //   calibrate (attention.py:173-189): global max and sum of exp, exact N-th
 //           largest logit by an 8-bit-per-pass radix select over the group,
 //           its probability as the threshold, top-N set (ties by position),
@@ -52,16 +55,18 @@ struct Misc {
   uint64_t empty[kMaxStages];  // K stage free again (UMMA commit)
   uint64_t tfull[2];           // TMEM accumulator ready (UMMA commit)
   uint64_t tempty[2];          // TMEM accumulator drained (4 epilogue warps)
-  uint64_t tdone;              // tail tiles scored by the 4 epilogue warps
   uint32_t tmem_slot;
   int abort;
-  uint32_t tag;        // exchange tag of this launch for the current group
-  uint32_t tkey[kMaxG];        // order-preserving keys of the tail max
-  float ered[4][kMaxG];        // per-epilogue-warp partial exp-sums / maxima
+  uint32_t tag;                // exchange tag of this launch for the current group
+  int stored;                  // tiles x 4 epilogue warps stored to SMEM (this item)
+  uint32_t tkey[kMaxG];        // order-preserving keys of the tail max (fp32 path)
+  float ered[2][kMaxG];        // per-helper-warp partial exp-sums
+  float emax[2][kMaxG];        // per-helper-warp partial maxima
+  int cntw[8][kMaxG];          // per-warp selection counts
   float m[kMaxG];      // tail max / global max
   float t[kMaxG];      // logit threshold / N-th logit
   float s[kMaxG];      // exp-sum
-  float aux[kMaxG];    // chunk-local stabiliser / p_N
+  float aux[kMaxG];    // stabiliser of the weights / p_N
   int i0[kMaxG];       // prefix / want
   int i1[kMaxG];       // keep / key prefix
   int i2[kMaxG];
@@ -82,7 +87,6 @@ struct Ring {
   uint32_t ms = 0, mph = 0;   // UMMA issuer stage / phase
   uint32_t mb = 0, mbph = 0;  // UMMA issuer TMEM buffer / phase
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
-  uint32_t tph = 0;           // tail-done barrier phase (epilogue warps)
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -107,6 +111,23 @@ __device__ __forceinline__ float funkey(uint32_t k) {
 }
 
 // ---------------------------------------------------------------------------
+// Packed pairs of 16-bit values
+// ---------------------------------------------------------------------------
+template <typename T> struct Pair;
+template <> struct Pair<__nv_bfloat16> {
+  using P = __nv_bfloat162;
+  __device__ __forceinline__ static P pack_rn(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  __device__ __forceinline__ static float2 unpack(P x) { return __bfloat1622float2(x); }
+  __device__ __forceinline__ static P sub(P a, P b) { return __hsub2(a, b); }
+};
+template <> struct Pair<__half> {
+  using P = __half2;
+  __device__ __forceinline__ static P pack_rn(float a, float b) { return __floats2half2_rn(a, b); }
+  __device__ __forceinline__ static float2 unpack(P x) { return __half22float2(x); }
+  __device__ __forceinline__ static P sub(P a, P b) { return __hsub2(a, b); }
+};
+
+// ---------------------------------------------------------------------------
 // Epoch-tagged exchange slots
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void slot_put(unsigned long long* p, uint32_t tag, uint32_t bits) {
@@ -124,6 +145,7 @@ __device__ __forceinline__ uint32_t slot_wait(const unsigned long long* p, unsig
   if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
   unsigned long long t0 = 0;
   for (uint32_t i = 1;; ++i) {
+    __nanosleep(32);
     v = slot_ld(p);
     if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
     if ((i & 255u) == 0) {
@@ -179,11 +201,11 @@ __device__ __forceinline__ float exp_term(float l, float m) {
 }
 
 // ---------------------------------------------------------------------------
-// Scoring on CUDA cores (fp32 path). 64-position sub-tiles of K are staged in
-// SMEM with cp.async (rows padded by 16 B); thread t scores position t % 64
-// for the heads of slice t / 64. Positions [a, a + cnt) are scored; with
-// max_only they only raise misc->tkey (the tail max), else they are stored at
-// sc[hl * CL + (pos - p0)].
+// Scoring on CUDA cores (fp32 path, or more than 16 query heads per key head).
+// 64-position sub-tiles of K are staged in SMEM with cp.async (rows padded by
+// 16 B); thread t scores position t % 64 for the heads of slice t / 64.
+// Positions [a, a + cnt) are scored; with max_only they only raise
+// misc->tkey (the tail max), else they are stored at sc[(pos - p0) * SH + hl].
 // ---------------------------------------------------------------------------
 template <typename T, int D>
 __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, int cnt, int p0, bool max_only,
@@ -193,7 +215,7 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
   constexpr int ROWB = D * (int)sizeof(T);
   constexpr int PITCH = ROWB + 16;
   constexpr int CPR = ROWB / 16;
-  const int CL = p.CL;
+  const int SH = p.sh;
   const T* kbase = reinterpret_cast<const T*>(p.k) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh;
   const int nsub = (cnt + SUB - 1) / SUB;
   const int h0 = kh * p.G;
@@ -256,7 +278,7 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
         if (hl < hend) {
           const float l = finalize_logit<T>(p, acc[hh], b, h0 + hl, pos);
           if (max_only) atomicMax(&misc->tkey[hl], fkey(l));
-          else sc[hl * CL + (pos - p0)] = Num<T>::from_f(l);
+          else sc[(pos - p0) * SH + hl] = Num<T>::from_f(l);
         }
       }
     }
@@ -265,26 +287,29 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
 }
 
 // ---------------------------------------------------------------------------
-// Scoring on the tensor cores (bf16 / fp16).
+// Scoring on the tensor cores (bf16 / fp16, G <= 16).
 //   warp 0 lane 0: TMA producer of 128 x D key tiles (ring of ns stages);
 //   warp 1 lane 0: UMMA issuer, D(128 x 16, fp32 in TMEM) = K_tile . Q^T;
-//   warps 4-7    : epilogue, lane = position, 16 columns = query-head slots.
-// The tile sequence is n_pre tail tiles (global tile indices pre0 ...), whose
-// logits only raise the tail max, then the chunk's own tiles. With the tail
-// max known, the epilogue accumulates the chunk's exp-sum (amortized) or its
-// maximum (other modes) per head into misc->ered.
-// The query operand (16 rows, zero padded beyond G) is written into SMEM in the
-// same 128-B swizzled K-major layout the TMA produces for the key tiles.
+//   warps 4-7    : epilogue, lane = position, 16 columns = query-head slots,
+//                  finalised in pairs, 32 B stored per position;
+//   warps 2-3    : helpers, per-head exp-sum (amortized) and maximum of each
+//                  stored tile, overlapped with the next tiles.
+// The tile sequence is n_pre tail tiles (global tile indices pre0 ...), stored
+// to the tail scratch, then the chunk's own tiles. The query operand (16 rows,
+// zero padded beyond G) is written into SMEM in the same 128-B swizzled
+// K-major layout the TMA produces for the key tiles.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int MODE>
 __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int n, int pre0, int n_pre,
-                               T* __restrict__ sc, uint8_t* __restrict__ qop, uint8_t* __restrict__ ring,
-                               Misc* misc, Ring& rg, uint32_t tmem_base) {
+                               T* __restrict__ sc, T* __restrict__ tsc, uint8_t* __restrict__ qop,
+                               uint8_t* __restrict__ ring, Misc* misc, Ring& rg, uint32_t tmem_base) {
+  using PT = Pair<T>;
+  using P2 = typename PT::P;
   constexpr int KB = D / 64;  // 128-byte K blocks per row
   constexpr uint32_t TILE_BYTES = 128u * D * 2u;
   constexpr uint32_t IDESC = umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.G, CL = p.CL, NS = p.ns;
+  const int G = p.G, NS = p.ns;
   const int h0 = kh * G;
   const int ntl = (n + 127) / 128;
   const int nseq = n_pre + ntl;
@@ -300,7 +325,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     for (int e = 0; e < 8; ++e) vals[e] = (h < G) ? src[e] : Num<T>::from_f(0.f);
     *reinterpret_cast<uint4*>(qop + kb * 2048 + h * 128 + ((c ^ (h & 7)) << 4)) = *reinterpret_cast<uint4*>(vals);
   }
-  for (int hl = threadIdx.x; hl < kMaxG; hl += kThreads) misc->tkey[hl] = 0u;
+  if (threadIdx.x == 0) misc->stored = 0;
   fence_proxy_async_smem();
   __syncthreads();
 
@@ -319,6 +344,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         for (int kb = 0; kb < KB; ++kb)
           tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
         ++issued;
+        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * 64 + 16 + q] = clock64();
         if (++rg.ps == (uint32_t)NS) {
           rg.ps = 0;
           rg.pph ^= 1u;
@@ -363,6 +389,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         last_b = rg.mb;
         last_ph = rg.mbph;
         ++issued;
+        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * 64 + 32 + q] = clock64();
         if (++rg.ms == (uint32_t)NS) {
           rg.ms = 0;
           rg.mph ^= 1u;
@@ -376,16 +403,11 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       if (issued) mbar_wait(&misc->tfull[last_b], last_ph, p.status);
     }
   } else if (warp >= 4) {
+    // epilogue: TMEM -> logits (reference rounding chain) -> SMEM, 32 B per position
     const int q4 = warp - 4;  // TMEM lane quarter of this warp
-    float m[16], acc[16];
-#pragma unroll
-    for (int hl = 0; hl < 16; ++hl) {
-      m[hl] = 0.f;
-      acc[hl] = (MODE == MODE_AMORTIZED) ? 0.f : -INFINITY;
-    }
-    bool ok = true;
+    const float scl = p.scaling;
     for (int q = 0; q < nseq; ++q) {
-      ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
+      bool ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
         if (lane == 0) misc->abort = 1;
@@ -401,47 +423,133 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         rg.eb = 0;
         rg.ebph ^= 1u;
       }
-      if (q < n_pre) {
-        // tail tile: raise the tail max of each head
-        const int pos = (pre0 + q) * 128 + q4 * 32 + lane;
-        const bool in_tail = pos >= tail_start && pos < p.L;
+      const bool pre = q < n_pre;
+      const int pl = pre ? (q * 128 + q4 * 32 + lane) : ((q - n_pre) * 128 + q4 * 32 + lane);
+      const int pos = pre ? (pre0 * 128 + pl) : (p0 + pl);
+      if (pre || pl < n) {
+        alignas(16) P2 outv[8];
+        if (p.mask == nullptr) {
 #pragma unroll
-        for (int hl = 0; hl < 16; ++hl) {
-          if (hl < G) {
-            float l = in_tail ? finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, pos) : -INFINITY;
-            l = warp_nanmax(l);
-            if (lane == 0) atomicMax(&misc->tkey[hl], fkey(l));
+          for (int jj = 0; jj < 8; ++jj) {
+            // bmm output in the dtype, * scaling in fp32, rounded again
+            const float2 f = PT::unpack(PT::pack_rn(__uint_as_float(r[2 * jj]), __uint_as_float(r[2 * jj + 1])));
+            outv[jj] = PT::pack_rn(__fmul_rn(f.x, scl), __fmul_rn(f.y, scl));
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int ha = min(2 * jj, G - 1), hb2 = min(2 * jj + 1, G - 1);
+            outv[jj] = PT::pack_rn(finalize_logit<T>(p, __uint_as_float(r[2 * jj]), b, h0 + ha, pos),
+                                   finalize_logit<T>(p, __uint_as_float(r[2 * jj + 1]), b, h0 + hb2, pos));
           }
         }
-        if (q == n_pre - 1) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&misc->tdone);
-          mbar_wait(&misc->tdone, rg.tph, p.status);
-          rg.tph ^= 1u;
-#pragma unroll
-          for (int hl = 0; hl < 16; ++hl) m[hl] = (hl < G) ? funkey(misc->tkey[hl]) : 0.f;
-        }
-        continue;
+        uint4* dst = reinterpret_cast<uint4*>((pre ? tsc : sc) + (size_t)pl * 16);
+        dst[0] = *reinterpret_cast<const uint4*>(&outv[0]);
+        dst[1] = *reinterpret_cast<const uint4*>(&outv[4]);
       }
-      const int pl = (q - n_pre) * 128 + q4 * 32 + lane;
-      if (pl < n) {
+      __syncwarp();
+      if (!pre && p.trace && blockIdx.x < 1024 && q - n_pre < 16 && q4 == 0 && lane == 0)
+        p.trace[blockIdx.x * 64 + 48 + (q - n_pre)] = clock64();
+      if (lane == 0) {
+        __threadfence_block();
+        atomicAdd(&misc->stored, 1);
+      }
+    }
+  } else if (warp == 2 || warp == 3) {
+    // helpers: tail max first (each helper warp over all tail positions), then
+    // the per-head exp-sum and maximum of every stored own tile
+    const int hw = warp - 2;
+    float m[16], s[16], mx[16];
 #pragma unroll
-        for (int hl = 0; hl < 16; ++hl) {
-          if (hl < G) {
-            const float l = finalize_logit<T>(p, __uint_as_float(r[hl]), b, h0 + hl, p0 + pl);
-            sc[hl * CL + pl] = Num<T>::from_f(l);
-            if constexpr (MODE == MODE_AMORTIZED) acc[hl] += exp_term<T>(l, m[hl]);
-            else acc[hl] = nanmax(acc[hl], l);
+    for (int hl = 0; hl < 16; ++hl) {
+      m[hl] = -INFINITY;
+      s[hl] = 0.f;
+      mx[hl] = -INFINITY;
+    }
+    auto wait_stored = [&](int target) {
+      if (*reinterpret_cast<volatile int*>(&misc->stored) >= target) return true;
+      unsigned long long t0 = 0;
+      for (uint32_t it = 1; *reinterpret_cast<volatile int*>(&misc->stored) < target; ++it) {
+        __nanosleep(64);
+        if (misc->abort) return false;
+        if ((it & 255u) == 0) {
+          const unsigned long long now = globaltimer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kWaitLimitNs) {
+            set_status(p.status, SAGA_STATUS_WAIT_TIMEOUT);
+            return false;
+          }
+        }
+      }
+      return true;
+    };
+    bool live = true;
+    if (n_pre > 0) {
+      live = wait_stored(4 * n_pre);
+      __threadfence_block();
+      for (int pr = lane; pr < n_pre * 128; pr += 32) {
+        const int gp = pre0 * 128 + pr;
+        if (gp >= tail_start && gp < p.L) {
+          const uint4* src = reinterpret_cast<const uint4*>(tsc + (size_t)pr * 16);
+          const uint4 u0 = src[0], u1 = src[1];
+          const P2* pp0 = reinterpret_cast<const P2*>(&u0);
+          const P2* pp1 = reinterpret_cast<const P2*>(&u1);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const float2 f = PT::unpack(jj < 4 ? pp0[jj] : pp1[jj - 4]);
+            m[2 * jj] = nanmax(m[2 * jj], f.x);
+            m[2 * jj + 1] = nanmax(m[2 * jj + 1], f.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int hl = 0; hl < 16; ++hl) m[hl] = warp_nanmax(m[hl]);
+    }
+    P2 m2[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) m2[jj] = PT::pack_rn(m[2 * jj], m[2 * jj + 1]);
+    for (int q = 0; q < ntl && live; ++q) {
+      live = wait_stored(4 * (n_pre + q + 1));
+      if (!live) break;
+      __threadfence_block();
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int pl = q * 128 + k * 64 + hw * 32 + lane;
+        if (pl < n) {
+          const uint4* src = reinterpret_cast<const uint4*>(sc + (size_t)pl * 16);
+          const uint4 u0 = src[0], u1 = src[1];
+          const P2* pp0 = reinterpret_cast<const P2*>(&u0);
+          const P2* pp1 = reinterpret_cast<const P2*>(&u1);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            if (2 * jj < G) {
+              const P2 l2 = jj < 4 ? pp0[jj] : pp1[jj - 4];
+              const float2 f = PT::unpack(l2);
+              mx[2 * jj] = fmaxf(mx[2 * jj], f.x);
+              mx[2 * jj + 1] = fmaxf(mx[2 * jj + 1], f.y);
+              if constexpr (MODE == MODE_AMORTIZED) {
+                // exp(round(l - m)) rounded, per head (attention.py:145)
+                const float2 d = PT::unpack(PT::sub(l2, m2[jj]));
+                const float2 e = PT::unpack(PT::pack_rn(__expf(d.x), __expf(d.y)));
+                s[2 * jj] += e.x;
+                s[2 * jj + 1] += e.y;
+              }
+            }
           }
         }
       }
     }
-    // per-warp partials of the exp-sum / maximum (reduced in fixed order later)
 #pragma unroll
     for (int hl = 0; hl < 16; ++hl) {
       if (hl < G) {
-        const float v = (MODE == MODE_AMORTIZED) ? warp_sum(acc[hl]) : warp_nanmax(acc[hl]);
-        if (lane == 0) misc->ered[q4][hl] = v;
+        const float sv = warp_sum(s[hl]);
+        const float mv = warp_max(mx[hl]);
+        if (lane == 0) {
+          misc->ered[hw][hl] = sv;
+          misc->emax[hw][hl] = mv;
+          if (hw == 0) misc->m[hl] = m[hl];
+        }
       }
     }
   }
@@ -505,8 +613,8 @@ __device__ __forceinline__ bool bit_of(const uint32_t* bits, int i) { return (bi
 // Weight of (local head hl, chunk position i) by mode: exp(l - stabiliser),
 // or for calibration the probability rounded to the dtype.
 template <typename T, int MODE>
-__device__ __forceinline__ float weight_of(const T* sc, int CL, const Misc* misc, int hl, int i) {
-  const float l = Num<T>::to_f(sc[hl * CL + i]);
+__device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc, int hl, int i) {
+  const float l = Num<T>::to_f(sc[i * SH + hl]);
   if constexpr (MODE == MODE_CALIBRATE)
     return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, misc->m[hl])), misc->s[hl]));
   else
@@ -523,9 +631,9 @@ constexpr int kSlotS = 0, kSlotCnt = 1, kSlotM = 2, kSlotL = 3, kSlotO = 4;
 // V gather of one item. For each value head of the group and each batch of up
 // to 8 of its query heads, the positions any of them selected form a list;
 // their value rows are fetched once (cp.async, 16 B per thread and request)
-// into SMEM, weighted per query head and accumulated in fp32 per warp, then
-// reduced across warps in a fixed order. The partial (m, l, o[D]) of every
-// head is published through the group's tagged slots.
+// into SMEM, weighted per query head and accumulated in fp32 per warp (values
+// and weights), then reduced across warps in a fixed order. The partial
+// (m, l, o[D]) of every head is published through the group's tagged slots.
 // ---------------------------------------------------------------------------
 template <typename T, int D, int MODE>
 __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, int p0, int n,
@@ -536,19 +644,10 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
   constexpr int CPR = ROWB / 16;
   constexpr bool kDense = (MODE == MODE_DENSE);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = p.G, Gv = p.Gv, CL = p.CL, nw = (n + 31) / 32;
+  const int G = p.G, Gv = p.Gv, CL = p.CL, SH = p.sh, nw = (n + 31) / 32;
   const int BR = p.sm.br;
   const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
   const uint32_t tag = misc->tag;
-
-  // l = sum of the weights per head (fixed order)
-  for (int hl = warp; hl < G; hl += kWarps) {
-    float s = 0.f;
-    for (int i = lane; i < n; i += 32)
-      if (kDense || bit_of(sel + hl * (CL / 32), i)) s += weight_of<T, MODE>(sc, CL, misc, hl, i);
-    s = warp_sum(s);
-    if (lane == 0) misc->lsum[hl] = s;
-  }
 
   // gather groups (value head, batch of <= 8 query heads) and their lists (warp 0)
   if (warp == 0) {
@@ -605,10 +704,13 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
                                                            (int64_t)vh * p.v_sh + (int64_t)p0 * p.v_sl);
     const int64_t vstride = p.v_sl * (int64_t)sizeof(T);
     float acc[8][EPL];
+    float accl[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < 8; ++i) {
+      accl[i] = 0.f;
 #pragma unroll
       for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
+    }
 
     for (int e0 = g0; e0 < g1; e0 += BR) {
       const int rows = min(BR, g1 - e0);
@@ -623,7 +725,7 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
         const int r = i >> 3, hh = i & 7;
         const uint32_t ent = list[e0 + r];
         float wv = 0.f;
-        if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, CL, misc, hb + hh, ent & 0xFFFF);
+        if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, SH, misc, hb + hh, ent & 0xFFFF);
         wbuf[i] = wv;
       }
       cp_async_wait<0>();
@@ -635,32 +737,41 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
         const float4 wb = *reinterpret_cast<const float4*>(wbuf + r * 8 + 4);
         const float wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-        for (int hh = 0; hh < 8; ++hh)
+        for (int hh = 0; hh < 8; ++hh) {
+          accl[hh] += wr[hh];
 #pragma unroll
           for (int i = 0; i < EPL; ++i) acc[hh][i] = fmaf(wr[hh], vf[i], acc[hh][i]);
+        }
       }
       __syncthreads();
     }
     // cross-warp reduction in a fixed order (work is free again)
     float* red = reinterpret_cast<float*>(work);
+    float* redl = red + kWarps * 8 * D;
 #pragma unroll
-    for (int hh = 0; hh < 8; ++hh)
+    for (int hh = 0; hh < 8; ++hh) {
 #pragma unroll
       for (int i = 0; i < EPL; ++i) red[(warp * 8 + hh) * D + lane * EPL + i] = acc[hh][i];
+      if (lane == 0) redl[warp * 8 + hh] = accl[hh];
+    }
     __syncthreads();
-    for (int o = threadIdx.x; o < nh * D; o += kThreads) {
-      const int hh = o / D, d = o % D;
+    for (int o = threadIdx.x; o < nh * (D + 1); o += kThreads) {
+      const int hh = o / (D + 1), d = o % (D + 1);
       float s = 0.f;
+      if (d < D) {
 #pragma unroll
-      for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
-      slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(s));
+        for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
+        slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(s));
+      } else {
+#pragma unroll
+        for (int wp = 0; wp < kWarps; ++wp) s += redl[wp * 8 + hh];
+        slot_put(slot_at(p, g, j, hb + hh, kSlotL), tag, __float_as_uint(s));
+      }
     }
     __syncthreads();
   }
-  for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+  for (int hl = threadIdx.x; hl < G; hl += kThreads)
     slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
-    slot_put(slot_at(p, g, j, hl, kSlotL), tag, __float_as_uint(misc->lsum[hl]));
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -774,6 +885,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   uint8_t* qop = smem + p.sm.qop;
   float* qf = reinterpret_cast<float*>(smem + p.sm.qop);
   T* sc = reinterpret_cast<T*>(smem + p.sm.scores);
+  T* tsc = reinterpret_cast<T*>(smem + p.sm.tail);
   uint32_t* sel = reinterpret_cast<uint32_t*>(smem + p.sm.sel);
   uint32_t* eqb = reinterpret_cast<uint32_t*>(smem + p.sm.eq);
   uint32_t* list = reinterpret_cast<uint32_t*>(smem + p.sm.list);
@@ -781,7 +893,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   uint8_t* work = smem + p.sm.work;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = p.G, C = p.C, CL = p.CL;
+  const int G = p.G, C = p.C, CL = p.CL, SH = p.sh;
   Ring rg;
   uint32_t tmem_base = 0;
 
@@ -794,7 +906,6 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       mbar_init(&misc->tfull[bb], 1);
       mbar_init(&misc->tempty[bb], 4);
     }
-    mbar_init(&misc->tdone, 4);
     misc->abort = 0;
     mbar_fence_init();
   }
@@ -820,9 +931,11 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     const int row0 = b * p.Hq + h0;
     const bool tracing = p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
 #define SAGA_TRACE(k) \
-  if (tracing) p.trace[blockIdx.x * 16 + (k)] = clock64();
+  if (tracing) p.trace[blockIdx.x * 64 + (k)] = clock64();
     SAGA_TRACE(0)
-    if (threadIdx.x == 0) misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
+    if constexpr (MODE != MODE_LOGITS) {  // the logits-only mode has no workspace
+      if (threadIdx.x == 0) misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
+    }
 
     // ---- fused append of the decode token (StaticLayer.update's index_copy_).
     // Every chunk of the group writes the new key row (the same values) before
@@ -848,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       fence_proxy_async_global();  // the appended rows are read back by TMA
     }
 
-    // ---- logits of the chunk (and, for amortized, the tail max first)
+    // ---- logits of the chunk (and, for amortized, the tail max) ----
     const int tail_start = p.L - p.tail;
     if constexpr (TC) {
       int pre0 = 0, n_pre = 0;
@@ -857,14 +970,10 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         n_pre = (p.L + kTile - 1) / kTile - pre0;
       }
       __syncthreads();
-      score_chunk_tc<T, D, MODE>(p, b, kh, p0, n, pre0, n_pre, sc, qop, work, misc, rg, tmem_base);
+      score_chunk_tc<T, D, MODE>(p, b, kh, p0, n, pre0, n_pre, sc, tsc, qop, work, misc, rg, tmem_base);
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-        if (MODE == MODE_AMORTIZED) {
-          misc->m[hl] = funkey(misc->tkey[hl]);
-          misc->s[hl] = ((misc->ered[0][hl] + misc->ered[1][hl]) + misc->ered[2][hl]) + misc->ered[3][hl];
-        } else {
-          misc->aux[hl] = nanmax(nanmax(misc->ered[0][hl], misc->ered[1][hl]), nanmax(misc->ered[2][hl], misc->ered[3][hl]));
-        }
+        misc->s[hl] = misc->ered[0][hl] + misc->ered[1][hl];
+        misc->aux[hl] = fmaxf(misc->emax[0][hl], misc->emax[1][hl]);  // chunk max
       }
       __syncthreads();
     } else {
@@ -881,19 +990,16 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         const float m = funkey(misc->tkey[hl]);
         float s = 0.f, mx = -INFINITY;
         for (int i = lane; i < n; i += 32) {
-          const float l = Num<T>::to_f(sc[hl * CL + i]);
+          const float l = Num<T>::to_f(sc[i * SH + hl]);
           if (MODE == MODE_AMORTIZED) s += exp_term<T>(l, m);
-          else mx = nanmax(mx, l);
+          mx = fmaxf(mx, l);
         }
         s = warp_sum(s);
-        mx = warp_nanmax(mx);
+        mx = warp_max(mx);
         if (lane == 0) {
-          if (MODE == MODE_AMORTIZED) {
-            misc->m[hl] = m;
-            misc->s[hl] = s;
-          } else {
-            misc->aux[hl] = mx;
-          }
+          misc->m[hl] = m;
+          misc->s[hl] = s;
+          misc->aux[hl] = mx;
         }
       }
       __syncthreads();
@@ -904,7 +1010,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       T* lo = reinterpret_cast<T*>(p.logits_out);
       for (int i = threadIdx.x; i < G * n; i += kThreads) {
         const int hl = i / n, pl = i % n;
-        lo[(int64_t)(row0 + hl) * p.lo_ld + p0 + pl] = sc[hl * CL + pl];
+        lo[(int64_t)(row0 + hl) * p.lo_ld + p0 + pl] = sc[pl * SH + hl];
       }
       __syncthreads();
       continue;
@@ -934,21 +1040,38 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         }
       }
       __syncthreads();
-      // strict selection x > t (triton_atopn.py:42) and per-chunk counts
-      for (int hl = warp; hl < G; hl += kWarps) {
-        const float t = misc->t[hl];
+      // strict selection x > t (triton_atopn.py:42): one 32-position word per
+      // warp step, one ballot per head, lane hl keeps head hl's word
+      {
+        float tl[kMaxG];
+#pragma unroll
+        for (int hl = 0; hl < kMaxG; ++hl) tl[hl] = (hl < G) ? misc->t[hl] : INFINITY;
+        int mycnt = 0;
+        for (int wi = warp; wi < nw; wi += kWarps) {
+          const int i = wi * 32 + lane;
+          uint32_t mine = 0;
+#pragma unroll
+          for (int hl = 0; hl < kMaxG; ++hl) {
+            if (hl < G) {
+              const bool pass = (i < n) && (Num<T>::to_f(sc[i * SH + hl]) > tl[hl]);
+              const uint32_t bits = __ballot_sync(0xffffffffu, pass);
+              if (lane == hl) mine = bits;
+            }
+          }
+          if (lane < G) {
+            sel[lane * (CL / 32) + wi] = mine;
+            mycnt += __popc(mine);
+          }
+        }
+        if (lane < G) misc->cntw[warp][lane] = mycnt;
+      }
+      __syncthreads();
+      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         int cnt = 0;
-        for (int w = 0; w < nw; ++w) {
-          const int i = w * 32 + lane;
-          const bool pass = (i < n) && (Num<T>::to_f(sc[hl * CL + i]) > t);
-          const uint32_t bits = __ballot_sync(0xffffffffu, pass);
-          if (lane == 0) sel[hl * (CL / 32) + w] = bits;
-          cnt += __popc(bits);
-        }
-        if (lane == 0) {
-          misc->i2[hl] = cnt;
-          slot_put(slot_at(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
-        }
+#pragma unroll
+        for (int wp = 0; wp < kWarps; ++wp) cnt += misc->cntw[wp][hl];
+        misc->i2[hl] = cnt;
+        slot_put(slot_at(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
       }
       __syncthreads();
       SAGA_TRACE(3)
@@ -975,17 +1098,20 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       __syncthreads();
       for (int hl = warp; hl < G; hl += kWarps) {
-        if (misc->i1[hl] < misc->i2[hl]) warp_trim_bits(sel + hl * (CL / 32), nw, misc->i1[hl]);
+        if (misc->i1[hl] < misc->i2[hl]) {
+          // capped chunk: drop the passing positions past K, and use the max
+          // of the kept logits as the stabiliser
+          warp_trim_bits(sel + hl * (CL / 32), nw, misc->i1[hl]);
+          float m = -INFINITY;
+          for (int i = lane; i < n; i += 32)
+            if (bit_of(sel + hl * (CL / 32), i)) m = fmaxf(m, Num<T>::to_f(sc[i * SH + hl]));
+          m = warp_max(m);
+          if (lane == 0) misc->aux[hl] = m;
+        }
         if (p.sel_idx_out && misc->i0[hl] < p.sel_ld)
           warp_write_positions(sel + hl * (CL / 32), nw, p0,
                                p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i0[hl],
                                max(0, min(misc->i1[hl], p.sel_ld - misc->i0[hl])));
-        // chunk-local stabiliser: max over the kept logits
-        float m = -INFINITY;
-        for (int i = lane; i < n; i += 32)
-          if (bit_of(sel + hl * (CL / 32), i)) m = fmaxf(m, Num<T>::to_f(sc[hl * CL + i]));
-        m = warp_max(m);
-        if (lane == 0) misc->aux[hl] = m;
       }
       __syncthreads();
       gather_item<T, D, MODE>(p, g, j, b, h0, p0, n, sc, sel, list, work, wbuf, misc);
@@ -1007,8 +1133,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         for (int i = threadIdx.x; i < G * 256; i += kThreads) hsm[i] = 0;
         __syncthreads();
         for (int i = threadIdx.x; i < G * n; i += kThreads) {
-          const int hl = i / n, pl = i % n;
-          const uint32_t key = Num<T>::key(Num<T>::to_f(sc[hl * CL + pl]));
+          const int hl = i % G, pl = i / G;
+          const uint32_t key = Num<T>::key(Num<T>::to_f(sc[pl * SH + hl]));
           const bool match = (pass == 0) || ((key >> (shift + 8)) == (uint32_t)misc->i1[hl]);
           if (match) atomicAdd(&hsm[hl * 256 + ((key >> shift) & 255u)], 1);
         }
@@ -1020,7 +1146,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
           for (int hl = warp; hl < G; hl += kWarps) {
             const float M = misc->m[hl];
             float s = 0.f;
-            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), M));
+            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(Num<T>::to_f(sc[i * SH + hl]), M));
             s = warp_sum(s);
             if (lane == 0) st[hl].s = s;
           }
@@ -1066,7 +1192,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         for (int w = 0; w < nw; ++w) {
           const int i = w * 32 + lane;
           float pr = 0.f;
-          if (i < n) pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(Num<T>::to_f(sc[hl * CL + i]), M)), S));
+          if (i < n) pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(Num<T>::to_f(sc[i * SH + hl]), M)), S));
           const uint32_t gb = __ballot_sync(0xffffffffu, (i < n) && pr > pN);
           const uint32_t eb = __ballot_sync(0xffffffffu, (i < n) && pr == pN);
           if (lane == 0) {
@@ -1199,9 +1325,10 @@ const void* pick_d_mode(int D, int mode) {
   }
 }
 
-const void* pick_kernel(int dt, int D, int mode) {
-  if (dt == SAGA_BF16) return pick_d_mode<__nv_bfloat16, true>(D, mode);
-  if (dt == SAGA_FP16) return pick_d_mode<__half, true>(D, mode);
+const void* pick_kernel(int dt, int D, int mode, bool tc) {
+  if (dt == SAGA_BF16)
+    return tc ? pick_d_mode<__nv_bfloat16, true>(D, mode) : pick_d_mode<__nv_bfloat16, false>(D, mode);
+  if (dt == SAGA_FP16) return tc ? pick_d_mode<__half, true>(D, mode) : pick_d_mode<__half, false>(D, mode);
   return pick_d_mode<float, false>(D, mode);
 }
 
@@ -1257,15 +1384,16 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   const int groups = a->B * a->Hk;
   const int ntiles = (a->L + kTile - 1) / kTile;
   const int es = esize_of(a->dtype);
-  const bool tc = (a->dtype != SAGA_FP32);
+  const bool tc = (a->dtype != SAGA_FP32) && G <= 16;
   const int ngg = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
-  // tensor-core path: one CTA per SM, deepest K ring that fits; fp32: two per SM
+  // tensor-core path: one CTA per SM, deepest K ring that fits; else two per SM
   const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
+  const int cbound = std::min(ntiles, 4096);
   int ns = tc ? kMaxStages : 2, max_tiles = 0;
   for (; ns >= 2; --ns) {
     max_tiles = 0;
     for (int t = 1; t <= ntiles; ++t) {
-      if (smem_layout(G, a->D, t * kTile, es, std::min(ntiles, 4096), tc, ns, ngg).total <= budget) max_tiles = t;
+      if (smem_layout(G, a->D, t * kTile, es, cbound, tc, ns, ngg).total <= budget) max_tiles = t;
       else break;
     }
     if (!tc || max_tiles >= std::min(ntiles, 8)) break;
@@ -1295,7 +1423,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   pl->nvh = ngg;
   pl->tc = tc;
   pl->cooperative = (mode != MODE_LOGITS);
-  const void* kfn = pick_kernel(a->dtype, a->D, mode);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, tc);
   if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm.total) != cudaSuccess) {
     *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(cudaGetLastError());
     return SAGA_ERR_CUDA;
@@ -1335,6 +1463,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   p.B = a->B; p.Hq = a->Hq; p.Hk = a->Hk; p.Hv = a->Hv; p.D = a->D; p.L = a->L;
   p.G = pl.G; p.Gv = pl.Gv;
   p.C = pl.C; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
+  p.sh = pl.G <= 16 ? 16 : 32;
   p.tail = std::min(kTail, a->L);
   if (mode == MODE_AMORTIZED) p.buf_k = std::min(2 * a->top_n, a->L);
   else if (mode == MODE_CALIBRATE) p.buf_k = std::min(a->top_n, a->L);
@@ -1388,7 +1517,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     }
   }
 
-  const void* kfn = pick_kernel(a->dtype, a->D, mode);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, pl.tc);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(kThreads);

@@ -32,7 +32,7 @@ constexpr int kMaxGatherGroups = 64;
 
 // Shared-memory carve of the fused kernel, in bytes from a 1024-aligned base.
 struct SmemLayout {
-  int misc, qop, scores, sel, eq, list, wbuf, work, total;
+  int misc, qop, scores, tail, sel, eq, list, wbuf, work, total;
   int work_bytes;  // K-tile ring / SIMT stages, then V rows, histograms, reductions
   int br;          // value rows per gather batch
 };
@@ -45,9 +45,10 @@ __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a *
 __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esize, int C, bool tc, int ns,
                                                  int nvh) {
   SmemLayout l;
+  const int SH = G <= 16 ? 16 : 32;  // head slots per position of the logits
   const int rowb = D * esize;
   int work = tc ? ns * 128 * rowb : 2 * 64 * (rowb + 16);
-  const int red = 8 * 8 * D * 4;
+  const int red = 8 * 8 * D * 4 + 8 * 8 * 4;  // per-warp values and weight sums
   const int hist = G * 256 * 4;
   // merge staging: (m, l) and scale per covered head and chunk, o per output and chunk
   const int per = (G * D + C - 1) / C;
@@ -65,7 +66,8 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   l.misc = off;   off += 4096;
   l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
   l.work = off;   off += work;
-  l.scores = off; off += align_up(G * CL * esize, 128);
+  l.scores = off; off += align_up(SH * CL * esize, 128);
+  l.tail = off;   off += tc ? 3 * 128 * 16 * esize : 0;  // logits of the <= 3 tail tiles
   l.sel = off;    off += align_up(G * (CL / 32) * 4, 128);
   l.eq = off;     off += align_up(G * (CL / 32) * 4, 128);
   l.list = off;   off += align_up(nvh * CL * 4, 128);
@@ -79,7 +81,7 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
 struct DecodeParams {
   CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
   int B, Hq, Hk, Hv, D, L, G, Gv;
-  int C, CL, items, tail, buf_k, ns, nvh;
+  int C, CL, items, tail, buf_k, ns, nvh, sh;
   const void* q; int64_t q_sb, q_sh;
   const void* k; int64_t k_sb, k_sh, k_sl;
   const void* v; int64_t v_sb, v_sh, v_sl;

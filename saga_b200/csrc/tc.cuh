@@ -43,20 +43,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or about `hint_ns` pass, without spending issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
 // Wait for the phase of `parity` to complete, at most kWaitLimitNs. Returns
 // false (and flags the status word) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-  // cheap polls first; the clock is read only every 1024 polls after that
-  for (int i = 0; i < 2048; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait_sleep(bar, parity, 1000000u)) return true;
   const unsigned long long t0 = globaltimer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+  while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
       if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
       return false;
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
