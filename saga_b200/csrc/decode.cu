@@ -62,6 +62,9 @@ struct Misc {
   uint32_t tkey[kMaxG];        // order-preserving keys of the tail max (fp32 path)
   float ered[2][kMaxG];        // per-helper-warp partial exp-sums
   float emax[2][kMaxG];        // per-helper-warp partial maxima
+  float esum4[4][16];          // per-epilogue-warp partial exp-sums (first head pairs)
+  float emax4[4][16];          // per-epilogue-warp partial maxima (first head pairs)
+  int mready;                  // tail max published by the helpers (this item)
   int cntw[8][kMaxG];          // per-warp selection counts
   float m[kMaxG];      // tail max / global max
   float t[kMaxG];      // logit threshold / N-th logit
@@ -79,7 +82,7 @@ struct Misc {
   int flag;
   int last;
 };
-static_assert(sizeof(Misc) <= 4096, "Misc must fit its 4 KB slot");
+static_assert(sizeof(Misc) <= 6144, "Misc must fit its 6 KB slot");
 
 // Per-thread pipeline positions kept across items (only role threads use theirs).
 struct Ring {
@@ -325,7 +328,10 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     for (int e = 0; e < 8; ++e) vals[e] = (h < G) ? src[e] : Num<T>::from_f(0.f);
     *reinterpret_cast<uint4*>(qop + kb * 2048 + h * 128 + ((c ^ (h & 7)) << 4)) = *reinterpret_cast<uint4*>(vals);
   }
-  if (threadIdx.x == 0) misc->stored = 0;
+  if (threadIdx.x == 0) {
+    misc->stored = 0;
+    misc->mready = 0;
+  }
   fence_proxy_async_smem();
   __syncthreads();
 
@@ -403,10 +409,43 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       if (issued) mbar_wait(&misc->tfull[last_b], last_ph, p.status);
     }
   } else if (warp >= 4) {
-    // epilogue: TMEM -> logits (reference rounding chain) -> SMEM, 32 B per position
+    // epilogue: TMEM -> logits (reference rounding chain) -> SMEM, 32 B per
+    // position; for amortized it also folds the first EJ head pairs of its own
+    // tiles into per-head exp-sums and maxima (the helpers take the rest)
     const int q4 = warp - 4;  // TMEM lane quarter of this warp
     const float scl = p.scaling;
+    const int EJ = (MODE == MODE_AMORTIZED) ? ((G + 1) / 2) / 2 : 0;
+    float es[16], em[16];
+    P2 m2[8];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      es[k] = 0.f;
+      em[k] = -INFINITY;
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) m2[jj] = PT::pack_rn(0.f, 0.f);
     for (int q = 0; q < nseq; ++q) {
+      if (MODE == MODE_AMORTIZED && q == n_pre) {
+        // the helpers publish the tail max once the tail tiles are stored
+        unsigned long long t0 = 0;
+        for (uint32_t it = 1; *reinterpret_cast<volatile int*>(&misc->mready) == 0; ++it) {
+          __nanosleep(64);
+          if (misc->abort) break;
+          if ((it & 255u) == 0) {
+            const unsigned long long now = globaltimer_ns();
+            if (t0 == 0) {
+              t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
+              set_status(p.status, SAGA_STATUS_WAIT_TIMEOUT);
+              break;
+            }
+          }
+        }
+        __threadfence_block();
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          if (jj < EJ) m2[jj] = PT::pack_rn(misc->m[2 * jj], misc->m[2 * jj + 1]);
+      }
       bool ok = mbar_wait(&misc->tfull[rg.eb], rg.ebph, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) {
@@ -446,6 +485,21 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         uint4* dst = reinterpret_cast<uint4*>((pre ? tsc : sc) + (size_t)pl * 16);
         dst[0] = *reinterpret_cast<const uint4*>(&outv[0]);
         dst[1] = *reinterpret_cast<const uint4*>(&outv[4]);
+        if (MODE == MODE_AMORTIZED && !pre) {
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            if (jj < EJ) {
+              const float2 f = PT::unpack(outv[jj]);
+              em[2 * jj] = fmaxf(em[2 * jj], f.x);
+              em[2 * jj + 1] = fmaxf(em[2 * jj + 1], f.y);
+              // exp(round(l - m)) rounded, per head (attention.py:145)
+              const float2 dd = PT::unpack(PT::sub(outv[jj], m2[jj]));
+              const float2 e = PT::unpack(PT::pack_rn(__expf(dd.x), __expf(dd.y)));
+              es[2 * jj] += e.x;
+              es[2 * jj + 1] += e.y;
+            }
+          }
+        }
       }
       __syncwarp();
       if (!pre && p.trace && blockIdx.x < 1024 && q - n_pre < 16 && q4 == 0 && lane == 0)
@@ -453,6 +507,19 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       if (lane == 0) {
         __threadfence_block();
         atomicAdd(&misc->stored, 1);
+      }
+    }
+    if (MODE == MODE_AMORTIZED) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        if (k < 2 * EJ) {
+          const float sv = warp_sum(es[k]);
+          const float mv = warp_max(em[k]);
+          if (lane == 0) {
+            misc->esum4[q4][k] = sv;
+            misc->emax4[q4][k] = mv;
+          }
+        }
       }
     }
   } else if (warp == 2 || warp == 3) {
@@ -505,7 +572,18 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
 #pragma unroll
       for (int hl = 0; hl < 16; ++hl) m[hl] = warp_nanmax(m[hl]);
+      if (hw == 0) {
+#pragma unroll
+        for (int hl = 0; hl < 16; ++hl)
+          if (lane == hl) misc->m[hl] = m[hl];
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_block();
+          atomicExch(&misc->mready, 1);
+        }
+      }
     }
+    const int EJ = (MODE == MODE_AMORTIZED) ? ((G + 1) / 2) / 2 : 0;
     P2 m2[8];
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) m2[jj] = PT::pack_rn(m[2 * jj], m[2 * jj + 1]);
@@ -523,7 +601,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
           const P2* pp1 = reinterpret_cast<const P2*>(&u1);
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
-            if (2 * jj < G) {
+            if (2 * jj < G && jj >= EJ) {
               const P2 l2 = jj < 4 ? pp0[jj] : pp1[jj - 4];
               const float2 f = PT::unpack(l2);
               mx[2 * jj] = fmaxf(mx[2 * jj], f.x);
@@ -548,7 +626,6 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         if (lane == 0) {
           misc->ered[hw][hl] = sv;
           misc->emax[hw][hl] = mv;
-          if (hw == 0) misc->m[hl] = m[hl];
         }
       }
     }
@@ -648,61 +725,110 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
   const int BR = p.sm.br;
   const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
   const uint32_t tag = misc->tag;
+  int* wtot = misc->cntw[0];  // per-warp scan totals (reused)
 
-  // gather groups (value head, batch of <= 8 query heads) and their lists (warp 0)
-  if (warp == 0) {
-    int ng = 0, pos_total = 0;
+  // gather groups: (value head, batch of <= 8 of its query heads)
+  if (threadIdx.x == 0) {
+    int ng = 0;
     for (int vh = vh_lo; vh <= vh_hi; ++vh) {
       const int a = max(h0, vh * Gv) - h0;
       const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
       for (int hb = a; hb < bnd && ng < kMaxGatherGroups; hb += 8) {
-        const int nh = min(8, bnd - hb);
-        if (lane == 0) {
-          misc->gstart[ng] = pos_total;
-          misc->gvh[ng] = vh;
-          misc->ghb[ng] = hb | (nh << 16);
-        }
-        if (kDense) {
-          const uint32_t all = (1u << nh) - 1u;
-          for (int i = lane; i < n; i += 32) list[pos_total + i] = (uint32_t)i | (all << 16);
-          pos_total += n;
-        } else {
-          for (int w0 = 0; w0 < nw; w0 += 32) {
-            const int ww = w0 + lane;
-            uint32_t u = 0;
-            if (ww < nw)
-              for (int hh = 0; hh < nh; ++hh) u |= sel[(hb + hh) * (CL / 32) + ww];
-            const int c = __popc(u);
-            const int incl = warp_incl_scan(c);
-            int o = pos_total + incl - c;
-            while (u) {
-              const int bit = __ffs(u) - 1;
-              u &= u - 1;
-              uint32_t hm = 0;
-              for (int hh = 0; hh < nh; ++hh) hm |= ((sel[(hb + hh) * (CL / 32) + ww] >> bit) & 1u) << hh;
-              list[o++] = (uint32_t)(ww * 32 + bit) | (hm << 16);
-            }
-            pos_total += __shfl_sync(0xffffffffu, incl, 31);
-          }
-        }
+        misc->gvh[ng] = vh;
+        misc->ghb[ng] = hb | (min(8, bnd - hb) << 16);
         ++ng;
       }
     }
-    if (lane == 0) {
-      misc->gstart[ng] = pos_total;
-      misc->ngroups = ng;
-    }
+    misc->ngroups = ng;
   }
   __syncthreads();
-
   const int ngroups = misc->ngroups;
+
+  // lists: one task per (group, 32-position word); a block-wide exclusive scan
+  // of the entry counts places every task's entries, ascending by position
+  // within each group. Entry = position | head mask << 16 | group << 24.
+  const int ntasks = ngroups * nw;
+  int running = 0;
+  for (int base = 0; base < ntasks; base += kThreads) {
+    const int task = base + threadIdx.x;
+    uint32_t u = 0, words[8];
+    int gi = 0, ww = 0, nh = 0;
+    if (task < ntasks) {
+      gi = task / nw;
+      ww = task % nw;
+      const int hb = misc->ghb[gi] & 0xFFFF;
+      nh = misc->ghb[gi] >> 16;
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) {
+        words[hh] = 0;
+        if (hh < nh) {
+          if (kDense) {
+            const int rem = n - ww * 32;
+            words[hh] = rem >= 32 ? 0xFFFFFFFFu : ((1u << rem) - 1u);
+          } else {
+            words[hh] = sel[(hb + hh) * (CL / 32) + ww];
+          }
+        }
+        u |= words[hh];
+      }
+    }
+    const int c = __popc(u);
+    const int incl = warp_incl_scan(c);
+    if (lane == 31) wtot[warp] = incl;
+    __syncthreads();
+    int before = running;
+    for (int w = 0; w < warp; ++w) before += wtot[w];
+    before += incl - c;
+    if (task < ntasks && ww == 0) misc->gstart[gi] = before;
+    int o = before;
+    while (u) {
+      const int bit = __ffs(u) - 1;
+      u &= u - 1;
+      uint32_t hm = 0;
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) hm |= ((words[hh] >> bit) & 1u) << hh;
+      list[o++] = (uint32_t)(ww * 32 + bit) | (hm << 16) | ((uint32_t)gi << 24);
+    }
+    int tot = 0;
+    for (int w = 0; w < kWarps; ++w) tot += wtot[w];
+    running += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) misc->gstart[ngroups] = running;
+  __syncthreads();
+  const int total = running;
+  const bool one_batch = total <= BR;
+
+  // issue the value rows of entries [e0, e0 + rows) into SMEM rows [0, rows),
+  // compute their weights meanwhile, and wait
+  auto load_rows = [&](int e0, int rows) {
+    for (int i = threadIdx.x; i < rows * CPR; i += kThreads) {
+      const int r = i / CPR, c = i % CPR;
+      const uint32_t ent = list[e0 + r];
+      const int vh = misc->gvh[ent >> 24];
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(
+          reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh +
+          (int64_t)(p0 + (int)(ent & 0xFFFFu)) * p.v_sl);
+      cp_async16(work + (size_t)r * ROWB + c * 16, src + c * 16, true);
+    }
+    cp_async_commit();
+    for (int i = threadIdx.x; i < rows * 8; i += kThreads) {
+      const int r = i >> 3, hh = i & 7;
+      const uint32_t ent = list[e0 + r];
+      const int gi = ent >> 24;
+      const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+      float wv = 0.f;
+      if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, SH, misc, hb + hh, ent & 0xFFFFu);
+      wbuf[i] = wv;
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+  };
+  if (one_batch && total > 0) load_rows(0, total);
+
   for (int gi = 0; gi < ngroups; ++gi) {
     const int g0 = misc->gstart[gi], g1 = misc->gstart[gi + 1];
-    const int vh = misc->gvh[gi];
     const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
-    const uint8_t* vrow0 = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb +
-                                                           (int64_t)vh * p.v_sh + (int64_t)p0 * p.v_sl);
-    const int64_t vstride = p.v_sl * (int64_t)sizeof(T);
     float acc[8][EPL];
     float accl[8];
 #pragma unroll
@@ -711,30 +837,19 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
 #pragma unroll
       for (int e = 0; e < EPL; ++e) acc[i][e] = 0.f;
     }
-
     for (int e0 = g0; e0 < g1; e0 += BR) {
       const int rows = min(BR, g1 - e0);
-      for (int i = threadIdx.x; i < rows * CPR; i += kThreads) {
-        const int r = i / CPR, c = i % CPR;
-        const int pos = list[e0 + r] & 0xFFFF;
-        cp_async16(work + (size_t)r * ROWB + c * 16, vrow0 + (int64_t)pos * vstride + c * 16, true);
+      int rbase = e0;  // SMEM row of entry e0
+      if (!one_batch) {
+        load_rows(e0, rows);
+        rbase = 0;
       }
-      cp_async_commit();
-      // weights of the batch while the rows land
-      for (int i = threadIdx.x; i < rows * 8; i += kThreads) {
-        const int r = i >> 3, hh = i & 7;
-        const uint32_t ent = list[e0 + r];
-        float wv = 0.f;
-        if (hh < nh && ((ent >> (16 + hh)) & 1u)) wv = weight_of<T, MODE>(sc, SH, misc, hb + hh, ent & 0xFFFF);
-        wbuf[i] = wv;
-      }
-      cp_async_wait<0>();
-      __syncthreads();
       for (int r = warp; r < rows; r += kWarps) {
+        const int rr = rbase + r;
         float vf[EPL];
-        loadNf<T, EPL>(reinterpret_cast<const T*>(work + (size_t)r * ROWB) + lane * EPL, vf);
-        const float4 wa = *reinterpret_cast<const float4*>(wbuf + r * 8);
-        const float4 wb = *reinterpret_cast<const float4*>(wbuf + r * 8 + 4);
+        loadNf<T, EPL>(reinterpret_cast<const T*>(work + (size_t)rr * ROWB) + lane * EPL, vf);
+        const float4 wa = *reinterpret_cast<const float4*>(wbuf + rr * 8);
+        const float4 wb = *reinterpret_cast<const float4*>(wbuf + rr * 8 + 4);
         const float wr[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
         for (int hh = 0; hh < 8; ++hh) {
@@ -743,32 +858,29 @@ __device__ void gather_item(const DecodeParams& p, int g, int j, int b, int h0, 
           for (int i = 0; i < EPL; ++i) acc[hh][i] = fmaf(wr[hh], vf[i], acc[hh][i]);
         }
       }
+      if (!one_batch) __syncthreads();
+    }
+    // cross-warp reduction in a fixed order, one head at a time, in the SMEM
+    // past the resident rows' weights
+    float* red = wbuf + (size_t)BR * 8;  // [kWarps][D + 1]
+    for (int hh = 0; hh < nh; ++hh) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k == hh) {
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) red[warp * (D + 1) + lane * EPL + i] = acc[k][i];
+          if (lane == 0) red[warp * (D + 1) + D] = accl[k];
+        }
+      }
+      __syncthreads();
+      for (int d = threadIdx.x; d <= D; d += kThreads) {
+        float s = 0.f;
+#pragma unroll
+        for (int wp = 0; wp < kWarps; ++wp) s += red[wp * (D + 1) + d];
+        slot_put(slot_at(p, g, j, hb + hh, d < D ? kSlotO + d : kSlotL), tag, __float_as_uint(s));
+      }
       __syncthreads();
     }
-    // cross-warp reduction in a fixed order (work is free again)
-    float* red = reinterpret_cast<float*>(work);
-    float* redl = red + kWarps * 8 * D;
-#pragma unroll
-    for (int hh = 0; hh < 8; ++hh) {
-#pragma unroll
-      for (int i = 0; i < EPL; ++i) red[(warp * 8 + hh) * D + lane * EPL + i] = acc[hh][i];
-      if (lane == 0) redl[warp * 8 + hh] = accl[hh];
-    }
-    __syncthreads();
-    for (int o = threadIdx.x; o < nh * (D + 1); o += kThreads) {
-      const int hh = o / (D + 1), d = o % (D + 1);
-      float s = 0.f;
-      if (d < D) {
-#pragma unroll
-        for (int wp = 0; wp < kWarps; ++wp) s += red[(wp * 8 + hh) * D + d];
-        slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(s));
-      } else {
-#pragma unroll
-        for (int wp = 0; wp < kWarps; ++wp) s += redl[wp * 8 + hh];
-        slot_put(slot_at(p, g, j, hb + hh, kSlotL), tag, __float_as_uint(s));
-      }
-    }
-    __syncthreads();
   }
   for (int hl = threadIdx.x; hl < G; hl += kThreads)
     slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
@@ -971,9 +1083,16 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       __syncthreads();
       score_chunk_tc<T, D, MODE>(p, b, kh, p0, n, pre0, n_pre, sc, tsc, qop, work, misc, rg, tmem_base);
+      const int ej2 = (MODE == MODE_AMORTIZED) ? 2 * (((G + 1) / 2) / 2) : 0;
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-        misc->s[hl] = misc->ered[0][hl] + misc->ered[1][hl];
-        misc->aux[hl] = fmaxf(misc->emax[0][hl], misc->emax[1][hl]);  // chunk max
+        if (hl < ej2) {  // heads folded by the epilogue warps
+          misc->s[hl] = ((misc->esum4[0][hl] + misc->esum4[1][hl]) + misc->esum4[2][hl]) + misc->esum4[3][hl];
+          misc->aux[hl] = fmaxf(fmaxf(misc->emax4[0][hl], misc->emax4[1][hl]),
+                                fmaxf(misc->emax4[2][hl], misc->emax4[3][hl]));
+        } else {
+          misc->s[hl] = misc->ered[0][hl] + misc->ered[1][hl];
+          misc->aux[hl] = fmaxf(misc->emax[0][hl], misc->emax[1][hl]);  // chunk max
+        }
       }
       __syncthreads();
     } else {
@@ -1043,19 +1162,29 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // strict selection x > t (triton_atopn.py:42): one 32-position word per
       // warp step, one ballot per head, lane hl keeps head hl's word
       {
-        float tl[kMaxG];
-#pragma unroll
-        for (int hl = 0; hl < kMaxG; ++hl) tl[hl] = (hl < G) ? misc->t[hl] : INFINITY;
         int mycnt = 0;
         for (int wi = warp; wi < nw; wi += kWarps) {
           const int i = wi * 32 + lane;
           uint32_t mine = 0;
+          for (int hs = 0; hs < G; hs += 16) {
+            // the position's 16 logits of this head block, two 16-byte loads
+            float lv[16];
+            if (i < n) {
+              const uint4* src = reinterpret_cast<const uint4*>(sc + (size_t)i * SH + hs);
+              load8f<T>(reinterpret_cast<const T*>(&src[0]), lv);
+              if (sizeof(T) == 2) load8f<T>(reinterpret_cast<const T*>(&src[1]), lv + 8);
+              else load8f<T>(sc + (size_t)i * SH + hs + 8, lv + 8);
+            } else {
 #pragma unroll
-          for (int hl = 0; hl < kMaxG; ++hl) {
-            if (hl < G) {
-              const bool pass = (i < n) && (Num<T>::to_f(sc[i * SH + hl]) > tl[hl]);
-              const uint32_t bits = __ballot_sync(0xffffffffu, pass);
-              if (lane == hl) mine = bits;
+              for (int k = 0; k < 16; ++k) lv[k] = -INFINITY;
+            }
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int hl = hs + k;
+              if (hl < G) {
+                const uint32_t bits = __ballot_sync(0xffffffffu, lv[k] > misc->t[hl]);
+                if (lane == hl) mine = bits;
+              }
             }
           }
           if (lane < G) {
@@ -1389,23 +1518,34 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   // tensor-core path: one CTA per SM, deepest K ring that fits; else two per SM
   const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
   const int cbound = std::min(ntiles, 4096);
-  int ns = tc ? kMaxStages : 2, max_tiles = 0;
-  for (; ns >= 2; --ns) {
-    max_tiles = 0;
+  const int target = tc ? di.sms : 2 * di.sms;
+  const int c_par = std::max(1, target / std::max(1, groups));
+  // Deepest K ring whose chunk still lets every group run in one wave; if no
+  // ring depth allows that, the deepest one that fits.
+  auto tiles_for = [&](int stages) {
+    int mt = 0;
     for (int t = 1; t <= ntiles; ++t) {
-      if (smem_layout(G, a->D, t * kTile, es, cbound, tc, ns, ngg).total <= budget) max_tiles = t;
+      if (smem_layout(G, a->D, t * kTile, es, cbound, tc, stages, ngg).total <= budget) mt = t;
       else break;
     }
-    if (!tc || max_tiles >= std::min(ntiles, 8)) break;
+    return mt;
+  };
+  int ns = tc ? kMaxStages : 2, max_tiles = tiles_for(ns);
+  if (tc) {
+    for (int s = kMaxStages; s >= 2; --s) {
+      const int mt = tiles_for(s);
+      if (mt > 0 && (ntiles + mt - 1) / mt <= c_par) {
+        ns = s;
+        max_tiles = mt;
+        break;
+      }
+    }
   }
-  if (ns < 2) ns = 2;
   if (max_tiles == 0) {
     *err = "shapes need more shared memory than one CTA has";
     return SAGA_ERR_UNSUPPORTED;
   }
   const int c_fit = (ntiles + max_tiles - 1) / max_tiles;
-  const int target = tc ? di.sms : 2 * di.sms;
-  const int c_par = std::max(1, target / std::max(1, groups));
   int C = std::max(c_fit, std::min(c_par, ntiles));
   int tiles = (ntiles + C - 1) / C;
   C = (ntiles + tiles - 1) / tiles;

@@ -61,17 +61,19 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   work = work > xchg ? work : xchg;
   work = align_up(work, 1024);
   int br = work / rowb;
-  br = br > 4096 ? 4096 : br;
+  br = br > 512 ? 512 : br;
   int off = 0;
-  l.misc = off;   off += 4096;
+  l.misc = off;   off += 6144;
   l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
   l.work = off;   off += work;
   l.scores = off; off += align_up(SH * CL * esize, 128);
-  l.tail = off;   off += tc ? 3 * 128 * 16 * esize : 0;  // logits of the <= 3 tail tiles
   l.sel = off;    off += align_up(G * (CL / 32) * 4, 128);
   l.eq = off;     off += align_up(G * (CL / 32) * 4, 128);
-  l.list = off;   off += align_up(nvh * CL * 4, 128);
-  l.wbuf = off;   off += align_up(br * 8 * 4, 128);
+  // gather lists; during scoring the same bytes hold the logits of the <= 3 tail tiles
+  const int list_b = nvh * CL * 4, tail_b = tc ? 3 * 128 * 16 * esize : 0;
+  l.list = off;   off += align_up(list_b > tail_b ? list_b : tail_b, 128);
+  l.tail = l.list;
+  l.wbuf = off;   off += align_up(br * 8 * 4, 128) + align_up(8 * (D + 1) * 4, 128);  // weights, reduction
   l.total = off + 1024;  // slack to align the dynamic base to 1024
   l.work_bytes = work;
   l.br = br;
