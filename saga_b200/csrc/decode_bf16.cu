@@ -1,0 +1,12 @@
+// Instantiations of the fused decode kernel for bf16 (one translation unit
+// per dtype keeps the builds parallel).
+#include "decode_kernel.cuh"
+
+namespace saga {
+
+const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask) {
+  if (tc) return mask ? pick_d_mode<__nv_bfloat16, true, true>(D, mode) : pick_d_mode<__nv_bfloat16, true, false>(D, mode);
+  return mask ? pick_d_mode<__nv_bfloat16, false, true>(D, mode) : pick_d_mode<__nv_bfloat16, false, false>(D, mode);
+}
+
+}  // namespace saga

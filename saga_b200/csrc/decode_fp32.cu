@@ -1,0 +1,11 @@
+// Instantiations of the fused decode kernel for fp32 (one translation unit
+// per dtype keeps the builds parallel).
+#include "decode_kernel.cuh"
+
+namespace saga {
+
+const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask) {
+  return mask ? pick_d_mode<float, false, true>(D, mode) : pick_d_mode<float, false, false>(D, mode);
+}
+
+}  // namespace saga

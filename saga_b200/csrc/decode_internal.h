@@ -32,7 +32,7 @@ constexpr int kMaxGatherGroups = 64;
 
 // Shared-memory carve of the fused kernel, in bytes from a 1024-aligned base.
 struct SmemLayout {
-  int misc, qop, scores, tail, sel, eq, list, wbuf, work, total;
+  int misc, qop, scores, tail, sel, eq, hmask, list, wbuf, work, xbuf, total;
   int work_bytes;  // K-tile ring / SIMT stages, then V rows, histograms, reductions
   int br;          // value rows per gather batch
 };
@@ -54,21 +54,25 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   const int per = (G * D + C - 1) / C;
   const int nhs = per / D + 2;
   const int merge = 4 * (nhs * C * 3 + per * C) + 256;
-  const int xchg = 4 * C * G + 256;  // per-chunk exchange staging
+  // per-chunk exchange staging, at the end of the work area: the count
+  // exchange runs while value rows are landing at its start
+  const int xchg = align_up(4 * C * G, 128);
   work = work > red ? work : red;
   work = work > hist ? work : hist;
   work = work > merge ? work : merge;
-  work = work > xchg ? work : xchg;
+  work = work > xchg + 8 * rowb ? work : xchg + 8 * rowb;
   work = align_up(work, 1024);
-  int br = work / rowb;
+  int br = (work - xchg) / rowb;
   br = br > 512 ? 512 : br;
   int off = 0;
   l.misc = off;   off += 6144;
   l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
   l.work = off;   off += work;
+  l.xbuf = l.work + work - xchg;
   l.scores = off; off += align_up(SH * CL * esize, 128);
   l.sel = off;    off += align_up(G * (CL / 32) * 4, 128);
   l.eq = off;     off += align_up(G * (CL / 32) * 4, 128);
+  l.hmask = off;  off += align_up(CL * 4, 128);  // selected heads of each position
   // gather lists; during scoring the same bytes hold the logits of the <= 3 tail tiles
   const int list_b = nvh * CL * 4, tail_b = tc ? 3 * 128 * 16 * esize : 0;
   l.list = off;   off += align_up(list_b > tail_b ? list_b : tail_b, 128);
