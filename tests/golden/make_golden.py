@@ -134,9 +134,12 @@ def run_case(A, tt, name, shape, seed, opts):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SAGA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SAGA_REFERENCE"),
+                    help="checkout of noamelata/SAGA (or set SAGA_REFERENCE)")
     ap.add_argument("--only", default=None)
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference <SAGA checkout> or set SAGA_REFERENCE")
     sys.path.insert(0, a.reference)
     import torch
     torch.manual_seed(0)
