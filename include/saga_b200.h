@@ -130,6 +130,20 @@ SAGA_API size_t saga_workspace_bytes(const SagaAttnArgs* args, int32_t op);
  * positions pass, the K lowest positions are kept. */
 SAGA_API int saga_atopn_decode(const SagaAttnArgs* args, void* stream);
 
+/* saga_atopn_decode without a caller workspace. It has no counterpart in the
+ * reference: it serves hosts that cannot allocate device memory at call time.
+ * The scratch is a fixed array of saga_noalloc_scratch_bytes() (8 MiB) in the
+ * library's own device memory, one per device; shapes that need more are
+ * refused with SAGA_ERR_WORKSPACE (args->workspace is ignored). Each call
+ * zero-fills the bytes it uses with one cudaMemsetAsync on `stream`. Calls on
+ * one device must not overlap on the GPU: they share the scratch. Make the
+ * first call on a device outside stream capture (it looks the array's address
+ * up once). Nothing is allocated. */
+SAGA_API int saga_atopn_decode_noalloc(const SagaAttnArgs* args, void* stream);
+
+/* Capacity in bytes of the static scratch of saga_atopn_decode_noalloc. */
+SAGA_API size_t saga_noalloc_scratch_bytes(void);
+
 /* Calibration step. Replaces approx_top_n_attention_amortized_cal
  * (attention.py:173-189): full softmax, exact top-min(N, L) probabilities,
  * thr_out[r] = the N-th largest probability (184-187), output from the

@@ -49,6 +49,8 @@ SIGNATURES = {
     "saga_workspace_bytes": (_sz, [ctypes.POINTER(SagaAttnArgs), _i32]),
     "saga_atopn_decode": (_i32, [ctypes.POINTER(SagaAttnArgs), _vp]),
     "saga_atopn_calibrate": (_i32, [ctypes.POINTER(SagaAttnArgs), _vp]),
+    "saga_atopn_decode_noalloc": (_i32, [ctypes.POINTER(SagaAttnArgs), _vp]),
+    "saga_noalloc_scratch_bytes": (_sz, []),
     "saga_dense_decode": (_i32, [ctypes.POINTER(SagaAttnArgs), _vp]),
     "saga_attn_logits": (_i32, [ctypes.POINTER(SagaAttnArgs), _vp]),
     "saga_transform_threshold": (_i32, [_i32, _vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp]),

@@ -95,6 +95,11 @@ int run_attn(const SagaAttnArgs* a, int op, void* stream) {
 
 }  // namespace
 
+namespace saga {
+// Error reporting for entry points defined in other files.
+int abi_fail(int code, const std::string& msg) { return fail(code, msg); }
+}  // namespace saga
+
 extern "C" {
 
 size_t saga_workspace_bytes(const SagaAttnArgs* args, int32_t op) {

@@ -1,0 +1,102 @@
+"""saga_atopn_decode_noalloc against saga_atopn_decode, through the C ABI.
+
+The file name sorts last so that pytest collects it after every other test:
+the static scratch is then reused after the regular entry points ran on other
+shapes, which is the case its per-call clearing exists for. It also passes
+when run alone.
+"""
+import ctypes
+
+import pytest
+import torch
+
+from saga_b200 import _lib as L
+from saga_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+# (B, L, Hq, Hk, Hv, D, N): config-2 head layout at a short context, and a
+# second shape so the two calls in a row use different scratch layouts
+SHAPES = [(2, 4096, 12, 1, 2, 128, 128), (3, 2944, 8, 2, 4, 64, 64)]
+
+
+def _inputs(shape, seed, dtype=torch.bfloat16):
+    B, Lk, Hq, Hk, Hv, D, _ = shape
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randn((B, Hq, 1, D), generator=g, device="cuda").to(dtype)
+    k = torch.randn((B, Hk, Lk, D), generator=g, device="cuda").to(dtype)
+    v = torch.randn((B, Hv, Lk, D), generator=g, device="cuda").to(dtype)
+    return q, k, v
+
+
+def _thresholds(shape, q, k, v):
+    B, _, Hq, _, _, _, N = shape
+    thr = torch.zeros(B * Hq, dtype=torch.float32, device="cuda")
+    ops.atopn_calibrate(q, k, v, None, thr, N)
+    return thr
+
+
+def _args(q, k, v, thr, N, out, status):
+    a = ops._attn_args(q, k, v, None, None)
+    a.top_n = N
+    a.thr_in = thr.data_ptr()
+    a.out, a.o_sb, a.o_sh = out.data_ptr(), out.stride(0), out.stride(1)
+    a.status = status.data_ptr()
+    return a
+
+
+def _regular(shape, q, k, v, thr):
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = _args(q, k, v, thr, shape[-1], out, status)
+    nbytes = L.lib.saga_workspace_bytes(ctypes.byref(a), L.SAGA_OP_ATOPN_DECODE)
+    assert nbytes > 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
+    L.check(L.lib.saga_atopn_decode(ctypes.byref(a), ctypes.c_void_p(ops._stream(q.device))), "saga_atopn_decode")
+    torch.cuda.synchronize()
+    return out, int(status.item())
+
+
+def _noalloc(shape, q, k, v, thr):
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = _args(q, k, v, thr, shape[-1], out, status)
+    a.workspace, a.workspace_bytes = None, 0  # ignored by the entry point
+    rc = L.lib.saga_atopn_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(ops._stream(q.device)))
+    L.check(rc, "saga_atopn_decode_noalloc")
+    torch.cuda.synchronize()
+    return out, int(status.item())
+
+
+def test_noalloc_matches_regular_two_calls_in_a_row():
+    cases = []
+    for i, shape in enumerate(SHAPES):
+        q, k, v = _inputs(shape, 100 + i)
+        thr = _thresholds(shape, q, k, v)
+        cases.append((shape, q, k, v, thr))
+    expected = [_regular(*c) for c in cases]
+    # two calls in a row on different shapes, then the first shape again
+    got = [_noalloc(*c) for c in cases] + [_noalloc(*cases[0])]
+    for (out, st), (ref, ref_st) in zip(got, expected + [expected[0]]):
+        assert st & L.STATUS_WAIT_TIMEOUT == 0
+        assert st == ref_st
+        assert torch.equal(out, ref)
+
+
+def test_noalloc_rejects_shapes_beyond_the_scratch():
+    cap = L.lib.saga_noalloc_scratch_bytes()
+    assert cap == 8 << 20
+    # 32 query heads per key head over many batch rows need more exchange
+    # slots than 8 MiB
+    shape = (32, 16384, 32, 1, 1, 128, 64)
+    q, k, v = _inputs(shape, 7)
+    thr = torch.zeros(shape[0] * shape[2], dtype=torch.float32, device="cuda")
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = _args(q, k, v, thr, shape[-1], out, status)
+    need = L.lib.saga_workspace_bytes(ctypes.byref(a), L.SAGA_OP_ATOPN_DECODE)
+    assert need > cap
+    rc = L.lib.saga_atopn_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(ops._stream(q.device)))
+    assert rc == L.SAGA_ERR_WORKSPACE
+    assert "static scratch" in L.lib.saga_last_error().decode()
