@@ -96,11 +96,13 @@ typedef struct SagaAttnArgs {
   void* workspace; size_t workspace_bytes; /* see saga_workspace_bytes */
   int32_t* status; /* device status word (SAGA_STATUS_*), or NULL */
 
-  /* Optional phase trace (NULL = off), int64 [1024][64]: CTA c < 1024 writes
-   * SM clock stamps (clock64) of its first work item at trace[c * 64 + k]:
-   * k = 0 start, 1 logits done, 2..6 after each inter-CTA exchange or the
-   * value gather, 7 item done; 16 + t / 32 + t / 48 + t: key tile t (< 16)
-   * issued by TMA / multiplied / stored by the epilogue. Diagnostics only. */
+  /* Optional phase trace (NULL = off), int64 [1024][128]. CTA c < 1024 writes
+   * stamps of its first work item into row c: column k < 16 = SM clock
+   * (clock64) at phase point k (0 start, 1 logits done, 7 item done, the rest
+   * after the exchanges and gather steps), column 64 + k = global timer (ns)
+   * at the same point; 16 + t / 32 + t / 48 + t = SM clock when key tile t
+   * (< 16) was issued by TMA / multiplied / stored; 127 = value rows
+   * gathered. Diagnostics only. */
   int64_t* trace;
 } SagaAttnArgs;
 

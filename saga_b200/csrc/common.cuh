@@ -14,6 +14,7 @@ constexpr int kThreads = 256;  // 8 warps per CTA in every kernel here
 constexpr int kWarps = kThreads / 32;
 constexpr int kTile = 128;     // positions per score tile
 constexpr int kTail = 256;     // attention.py:136, tail_size of the max estimate
+constexpr int kTraceCols = 128;  // int64 stamps per CTA in the optional phase trace
 constexpr unsigned long long kWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s
 
 // ---------------------------------------------------------------------------

@@ -188,6 +188,9 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   p.G = pl.G; p.Gv = pl.Gv;
   p.C = pl.C; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
   p.sh = pl.G <= 16 ? 16 : 32;
+  p.tmem_cols = 32;
+  if (uses_tc_pv(pl.tc, a->D))
+    while (p.tmem_cols < 16 * pl.nvh) p.tmem_cols *= 2;  // nvh <= 16 on this path: at most 256
   p.tail = std::min(kTail, a->L);
   if (mode == MODE_AMORTIZED) p.buf_k = std::min(2 * a->top_n, a->L);
   else if (mode == MODE_CALIBRATE) p.buf_k = std::min(a->top_n, a->L);

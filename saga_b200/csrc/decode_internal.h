@@ -34,8 +34,13 @@ constexpr int kMaxGatherGroups = 64;
 struct SmemLayout {
   int misc, qop, scores, tail, sel, eq, hmask, list, wbuf, work, xbuf, total;
   int work_bytes;  // K-tile ring / SIMT stages, then V rows, histograms, reductions
-  int br;          // value rows per gather batch
+  int br;          // value rows per gather batch (CUDA-core P.V)
+  int brw;         // value-row slots per pass of the tensor-core P.V (multiple of 16; 0 = not used)
 };
+
+// The tensor-core P.V (tcgen05, V rows as the M = head_dim operand) serves
+// 16-bit types at head_dim 128 on the tensor-core scorer path.
+__host__ __device__ constexpr bool uses_tc_pv(bool tc, int D) { return tc && D == 128; }
 
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
@@ -60,10 +65,13 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   work = work > red ? work : red;
   work = work > hist ? work : hist;
   work = work > merge ? work : merge;
-  work = work > xchg + 8 * rowb ? work : xchg + 8 * rowb;
+  work = work > xchg + 16 * rowb ? work : xchg + 16 * rowb;  // at least one 16-row P.V step
   work = align_up(work, 1024);
   int br = (work - xchg) / rowb;
   br = br > 512 ? 512 : br;
+  const bool tcpv = uses_tc_pv(tc, D);
+  // 16-row units of 8-row x 256-B swizzle-atom pairs below the exchange staging
+  const int brw = tcpv ? ((work - xchg) / (16 * rowb)) * 16 : 0;
   int off = 0;
   l.misc = off;   off += 6144;
   l.qop = off;    off += align_up(tc ? (D / 64) * 2048 : G * D * 4, 1024);
@@ -77,10 +85,16 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   const int list_b = nvh * CL * 4, tail_b = tc ? 3 * 128 * 16 * esize : 0;
   l.list = off;   off += align_up(list_b > tail_b ? list_b : tail_b, 128);
   l.tail = l.list;
-  l.wbuf = off;   off += align_up(br * 8 * 4, 128) + align_up(8 * (D + 1) * 4, 128);  // weights, reduction
+  if (tcpv) {  // bf16/fp16 weights, K-major 128-B swizzle blocks of 16 head slots x 64 rows
+    off = align_up(off, 1024);
+    l.wbuf = off;  off += align_up((brw + 63) / 64 * 2048, 1024);
+  } else {     // fp32 weights [br][8], then the cross-warp reduction buffer
+    l.wbuf = off;  off += align_up(br * 8 * 4, 128) + align_up(8 * (D + 1) * 4, 128);
+  }
   l.total = off + 1024;  // slack to align the dynamic base to 1024
   l.work_bytes = work;
   l.br = br;
+  l.brw = brw;
   return l;
 }
 
@@ -88,6 +102,7 @@ struct DecodeParams {
   CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
   int B, Hq, Hk, Hv, D, L, G, Gv;
   int C, CL, items, tail, buf_k, ns, nvh, sh;
+  int tmem_cols;  // TMEM columns per CTA: the scorer's 2 x 16, or 16 per gather group for the P.V
   const void* q; int64_t q_sb, q_sh;
   const void* k; int64_t k_sb, k_sh, k_sl;
   const void* v; int64_t v_sb, v_sh, v_sl;

@@ -76,9 +76,15 @@ struct Misc {
   int i2[kMaxG];
   int i3[kMaxG];
   float lsum[kMaxG];
+  float thr[kMaxG];     // softmax-space thresholds of the rows (amortized)
   int gstart[kMaxGatherGroups + 1];  // gather groups: list ranges
-  int gvh[kMaxGatherGroups];
-  int ghb[kMaxGatherGroups];
+  int gvh[kMaxGatherGroups];         // gather group -> value head
+  int ghb[kMaxGatherGroups];         // first local head | head count << 16
+  uint32_t gmask[kMaxGatherGroups];  // local heads of the gather group as a bit mask
+  int wsum[kWarps];                  // per-warp totals of a block scan
+  int gpad[kMaxGatherGroups + 1];    // tensor-core P.V: first row slot of each gather group (16-aligned)
+  float lacc[16 * 8];                // tensor-core P.V: weight sums per (gather group, head)
+  uint64_t pvbar;                    // tensor-core P.V: a pass's MMAs completed
   int ngroups;
   int flag;
   int last;
@@ -92,6 +98,15 @@ struct Ring {
   uint32_t mb = 0, mbph = 0;  // UMMA issuer TMEM buffer / phase
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
 };
+
+// Phase stamp k < 16 of the optional trace: SM clock at column k, global
+// timer (ns, comparable across SMs) at column 64 + k.
+__device__ __forceinline__ void trace_stamp(const DecodeParams& p, int k) {
+  if (p.trace && blockIdx.x < 1024) {
+    p.trace[blockIdx.x * kTraceCols + k] = clock64();
+    p.trace[blockIdx.x * kTraceCols + 64 + k] = (long long)globaltimer_ns();
+  }
+}
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
@@ -118,17 +133,27 @@ __device__ __forceinline__ float funkey(uint32_t k) {
 // Packed pairs of 16-bit values
 // ---------------------------------------------------------------------------
 template <typename T> struct Pair;
+// `pack_rd` rounds toward -inf: for any 16-bit value x and float t,
+// x > t  <=>  x > round_down(t), so a threshold compare can run on pairs.
 template <> struct Pair<__nv_bfloat16> {
   using P = __nv_bfloat162;
   __device__ __forceinline__ static P pack_rn(float a, float b) { return __floats2bfloat162_rn(a, b); }
+  __device__ __forceinline__ static P pack_rd(float a, float b) {
+    return __halves2bfloat162(__float2bfloat16_rd(a), __float2bfloat16_rd(b));
+  }
   __device__ __forceinline__ static float2 unpack(P x) { return __bfloat1622float2(x); }
   __device__ __forceinline__ static P sub(P a, P b) { return __hsub2(a, b); }
+  __device__ __forceinline__ static uint32_t gt_mask(P a, P b) { return __hgt2_mask(a, b); }
 };
 template <> struct Pair<__half> {
   using P = __half2;
   __device__ __forceinline__ static P pack_rn(float a, float b) { return __floats2half2_rn(a, b); }
+  __device__ __forceinline__ static P pack_rd(float a, float b) {
+    return __halves2half2(__float2half_rd(a), __float2half_rd(b));
+  }
   __device__ __forceinline__ static float2 unpack(P x) { return __half22float2(x); }
   __device__ __forceinline__ static P sub(P a, P b) { return __hsub2(a, b); }
+  __device__ __forceinline__ static uint32_t gt_mask(P a, P b) { return __hgt2_mask(a, b); }
 };
 
 // ---------------------------------------------------------------------------
@@ -143,41 +168,50 @@ __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* 
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// Wait until the slot carries `tag`; returns its 32-bit value (bounded wait).
-__device__ __forceinline__ uint32_t slot_wait(const unsigned long long* p, unsigned long long v, uint32_t tag,
-                                              int* status) {
-  if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
-  unsigned long long t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    __nanosleep(32);
-    v = slot_ld(p);
-    if ((uint32_t)(v >> 32) == tag) return (uint32_t)v;
-    if ((i & 255u) == 0) {
-      const unsigned long long now = globaltimer_ns();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitLimitNs) {
-        if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
-        return (uint32_t)v;
-      }
-    }
-  }
-}
-// All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i],
-// issuing 8 independent loads per thread before waiting on any of them.
+// All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i].
+// Each thread keeps up to 8 loads in flight and re-polls all of its pending
+// slots together, so a late publisher costs one round trip, not one per slot.
+// Bounded: after kWaitLimitNs the status word gets SAGA_STATUS_WAIT_TIMEOUT
+// and the stale values are used.
 template <typename AddrFn>
 __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t tag, uint32_t* dst, int* status) {
   for (int base = threadIdx.x; base < count; base += kThreads * 8) {
     unsigned long long v[8];
+    uint32_t pending = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int i = base + k * kThreads;
       v[k] = (i < count) ? slot_ld(addr(i)) : 0ull;
+      if (i < count) pending |= 1u << k;
     }
+    unsigned long long t0 = 0;
+    for (uint32_t it = 1;; ++it) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int i = base + k * kThreads;
-      if (i < count) dst[i] = slot_wait(addr(i), v[k], tag, status);
+      for (int k = 0; k < 8; ++k) {
+        if ((pending >> k) & 1u) {
+          if ((uint32_t)(v[k] >> 32) == tag) {
+            dst[base + k * kThreads] = (uint32_t)v[k];
+            pending &= ~(1u << k);
+          }
+        }
+      }
+      if (!pending) break;
+      if ((it & 255u) == 0) {
+        const unsigned long long now = globaltimer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitLimitNs) {
+          if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if ((pending >> k) & 1u) dst[base + k * kThreads] = (uint32_t)v[k];
+          break;
+        }
+      }
+      __nanosleep(32);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if ((pending >> k) & 1u) v[k] = slot_ld(addr(base + k * kThreads));
     }
   }
 }
@@ -352,7 +386,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         for (int kb = 0; kb < KB; ++kb)
           tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
         ++issued;
-        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * 64 + 16 + q] = clock64();
+        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * kTraceCols + 16 + q] = clock64();
         if (++rg.ps == (uint32_t)NS) {
           rg.ps = 0;
           rg.pph ^= 1u;
@@ -397,7 +431,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         last_b = rg.mb;
         last_ph = rg.mbph;
         ++issued;
-        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * 64 + 32 + q] = clock64();
+        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * kTraceCols + 32 + q] = clock64();
         if (++rg.ms == (uint32_t)NS) {
           rg.ms = 0;
           rg.mph ^= 1u;
@@ -497,7 +531,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
       __syncwarp();
       if (!pre && p.trace && blockIdx.x < 1024 && q - n_pre < 16 && q4 == 0 && lane == 0)
-        p.trace[blockIdx.x * 64 + 48 + (q - n_pre)] = clock64();
+        p.trace[blockIdx.x * kTraceCols + 48 + (q - n_pre)] = clock64();
       if (!pre && lane == 0) {
         __threadfence_block();
         atomicAdd(&misc->stored, 1);
@@ -717,12 +751,15 @@ __device__ __forceinline__ bool bit_of(const uint32_t* bits, int i) { return (bi
 // Weight of (local head hl, chunk position i) by mode: exp(l - stabiliser),
 // or for calibration the probability rounded to the dtype.
 template <typename T, int MODE>
-__device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc, int hl, int i) {
-  const float l = Num<T>::to_f(sc[i * SH + hl]);
+__device__ __forceinline__ float weight_from_logit(float l, const Misc* misc, int hl) {
   if constexpr (MODE == MODE_CALIBRATE)
     return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, misc->m[hl])), misc->s[hl]));
   else
     return __expf(l - misc->aux[hl]);
+}
+template <typename T, int MODE>
+__device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc, int hl, int i) {
+  return weight_from_logit<T, MODE>(Num<T>::to_f(sc[i * SH + hl]), misc, hl);
 }
 
 // Slot address: group g, chunk c, local head hl, field k.
@@ -760,68 +797,434 @@ __device__ __forceinline__ void issue_rows(const DecodeParams& p, int b, int p0,
   cp_async_commit();
 }
 
-template <typename T, int D, int MODE>
-__device__ void gather_begin(const DecodeParams& p, int b, int h0, int p0, int n, const uint32_t* __restrict__ hmask,
-                             uint32_t* __restrict__ list, int* __restrict__ tcnt, int* __restrict__ toff,
-                             uint8_t* __restrict__ work, Misc* misc) {
-  constexpr bool kDense = (MODE == MODE_DENSE);
+// Tensor-core P.V operand layouts (head_dim 128, 16-bit values):
+//  * value rows: row slot s, 16-byte segment sg (8 elements) -> byte offset
+//    in the MN-major 128-B swizzle layout: 8-slot groups of two 1024-B atoms
+//    (elements 0-63 and 64-127 of the row), the segment index XOR-ed with s % 8;
+//  * weights: slot s, head slot n (16 per gather group, the unused ones zero)
+//    -> byte offset in the K-major 128-B swizzle layout: blocks of 64 slots x
+//    16 head slots, one 128-B row per head slot.
+__device__ __forceinline__ int pv_row_off(int s, int sg) {
+  return (s >> 3) * 2048 + (sg >> 3) * 1024 + (s & 7) * 128 + (((sg & 7) ^ (s & 7)) << 4);
+}
+__device__ __forceinline__ int pv_w_off(int s, int n) {
+  return (s >> 6) * 2048 + (n >> 3) * 1024 + (n & 7) * 128 + ((((s & 63) >> 3) ^ (n & 7)) << 4) + (s & 7) * 2;
+}
+// Gather group holding row slot s (groups are contiguous, ascending).
+__device__ __forceinline__ int pv_group_of(const Misc* misc, int ngroups, int s) {
+  int gi = 0;
+  while (gi + 1 < ngroups && misc->gpad[gi + 1] <= s) ++gi;
+  return gi;
+}
+
+// Copies of the value rows of global row slots [s0, s1) into pass slots
+// s - pbase: rows of real entries from the cache, padding slots zero-filled.
+// RPI = 2 rows per warp instruction, 16 segments each.
+template <typename T>
+__device__ __forceinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0, const uint32_t* __restrict__ list,
+                                              uint8_t* __restrict__ work, const Misc* misc, int ngroups, int s0,
+                                              int s1, int pbase) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = p.G, Gv = p.Gv, nw = (n + 31) / 32;
-  const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
-  if (threadIdx.x == 0) {
-    int ng = 0;
-    for (int vh = vh_lo; vh <= vh_hi; ++vh) {
-      const int a = max(h0, vh * Gv) - h0;
-      const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
-      for (int hb = a; hb < bnd && ng < kMaxGatherGroups; hb += 8) {
-        misc->gvh[ng] = vh;
-        misc->ghb[ng] = hb | (min(8, bnd - hb) << 16);
-        ++ng;
+  const int sub = lane >> 4, sg = lane & 15;
+  const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)p0 * p.v_sl;
+  for (int gi = 0; gi < ngroups; ++gi) {
+    const int a = max(misc->gpad[gi], s0), z = min(misc->gpad[gi + 1], s1);
+    if (a >= z) continue;
+    const int e0 = misc->gstart[gi], rows = misc->gstart[gi + 1] - e0, gbase = misc->gpad[gi];
+    const T* vg = vb + (int64_t)misc->gvh[gi] * p.v_sh;
+#pragma unroll 2
+    for (int s = a + warp * 2 + sub; s < z; s += kWarps * 2) {
+      const int r = s - gbase;
+      uint8_t* dst = work + pv_row_off(s - pbase, sg);
+      if (r < rows) {
+        const int pos = (int)(list[e0 + r] & 0xFFFFu);
+        cp_async16(dst, vg + (int64_t)pos * p.v_sl + sg * 8, true);
+      } else {
+        cp_async16(dst, vg, false);  // zero row: padding of the 16-row MMA step
       }
     }
-    misc->ngroups = ng;
   }
-  __syncthreads();
+}
+
+// Weights of the P.V operand for pass slots [0, pn) (global slots ps0 + ...):
+// one task per (8-slot chunk, head slot) computes 8 weights and stores them as
+// one 16-byte K-major segment. Head slots past the group's heads, padding
+// slots and unselected (row, head) pairs get 0. With `capped_only`, only the
+// heads whose chunk was capped at K (keep < passing) are recomputed.
+template <typename T, int MODE>
+__device__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
+                           const uint32_t* __restrict__ list, uint8_t* __restrict__ wpv, const Misc* misc,
+                           int ngroups, int ps0, int pn, bool capped_only) {
+  constexpr bool kDense = (MODE == MODE_DENSE);
+  const int SH = p.sh;
+  for (int i = threadIdx.x; i < (pn >> 3) * 16; i += kThreads) {
+    const int c8 = i >> 4, nn = i & 15;
+    const int ps = c8 * 8, gs = ps0 + ps;
+    const int gi = pv_group_of(misc, ngroups, gs);
+    const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+    const int hl = hb + nn;
+    if (capped_only && (nn >= nh || misc->i1[hl] >= misc->i2[hl])) continue;
+    const int e0 = misc->gstart[gi], rows = misc->gstart[gi + 1] - e0;
+    const int r0 = gs - misc->gpad[gi];
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (nn < nh && r0 < rows) {
+      // all loads first (indices clamped to a real row), so the 8 chains overlap
+      int pos[8];
+      uint32_t hm[8];
+      float l[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) pos[k] = (int)(list[e0 + min(r0 + k, rows - 1)] & 0xFFFFu);
+      if constexpr (!kDense) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) hm[k] = hmask[pos[k]];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) l[k] = Num<T>::to_f(sc[pos[k] * SH + hl]);
+      T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const bool on = (r0 + k < rows) && (kDense || ((hm[k] >> hl) & 1u));
+        e[k] = Num<T>::from_f(on ? weight_from_logit<T, MODE>(l[k], misc, hl) : 0.f);
+      }
+    }
+    *reinterpret_cast<uint4*>(wpv + pv_w_off(ps, nn)) = u;
+  }
+}
+
+// Gather groups of an item: (value head, <= 8 of its query heads in this key
+// group). One thread.
+__device__ __forceinline__ void plan_gather_groups(const DecodeParams& p, int h0, Misc* misc) {
+  const int G = p.G, Gv = p.Gv;
+  const int vh_lo = h0 / Gv, vh_hi = (h0 + G - 1) / Gv;
+  int ng = 0;
+  for (int vh = vh_lo; vh <= vh_hi; ++vh) {
+    const int a = max(h0, vh * Gv) - h0;
+    const int bnd = min(h0 + G, (vh + 1) * Gv) - h0;
+    for (int hb = a; hb < bnd && ng < kMaxGatherGroups; hb += 8) {
+      const int nh = min(8, bnd - hb);
+      misc->gvh[ng] = vh;
+      misc->ghb[ng] = hb | (nh << 16);
+      misc->gmask[ng] = ((1u << nh) - 1u) << hb;
+      ++ng;
+    }
+  }
+  misc->ngroups = ng;
+}
+
+// Strict selection of one chunk: hmask[i] = heads whose logit at position i
+// exceeds misc->t (bit hl = local head hl), for i < nw * 32 (zero past n), and
+// misc->cntw[warp][hl] = the warp's count of passing positions of head hl.
+template <typename T>
+__device__ __forceinline__ void select_heads(const T* __restrict__ sc, int SH, int G, int n, int nw, Misc* misc,
+                                             uint32_t* __restrict__ hmask) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if constexpr (sizeof(T) == 2) {
+    // pairs of heads per compare; counts packed two per word (16-bit halves)
+    using PT = Pair<T>;
+    using P = typename PT::P;
+    P t2[16];
+    uint32_t c2[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float ta = (2 * k < G) ? misc->t[2 * k] : INFINITY;  // padded slots never pass
+      const float tb = (2 * k + 1 < G) ? misc->t[2 * k + 1] : INFINITY;
+      t2[k] = PT::pack_rd(ta, tb);
+      c2[k] = 0u;
+    }
+    const int npairs = SH / 2;
+    for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
+      uint32_t bits = 0;
+      if (i < n) {
+#pragma unroll
+        for (int hsb = 0; hsb < 2; ++hsb) {
+          if (hsb * 8 < npairs) {
+            const uint4* row = reinterpret_cast<const uint4*>(sc + (size_t)i * SH + hsb * 16);
+            const uint4 u0 = row[0], u1 = row[1];
+            const P* pa = reinterpret_cast<const P*>(&u0);
+            const P* pb = reinterpret_cast<const P*>(&u1);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t m = PT::gt_mask(k < 4 ? pa[k] : pb[k - 4], t2[hsb * 8 + k]) & 0x00010001u;
+              c2[hsb * 8 + k] += m;
+              bits |= ((m | (m >> 15)) & 3u) << (hsb * 16 + 2 * k);
+            }
+          }
+        }
+      }
+      hmask[i] = bits;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c2[k] = (uint32_t)warp_sum_i((int)c2[k]);
+    if (npairs > 8) {
+#pragma unroll
+      for (int k = 8; k < 16; ++k) c2[k] = (uint32_t)warp_sum_i((int)c2[k]);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        if (2 * k < G) misc->cntw[warp][2 * k] = (int)(c2[k] & 0xFFFFu);
+        if (2 * k + 1 < G) misc->cntw[warp][2 * k + 1] = (int)(c2[k] >> 16);
+      }
+    }
+  } else {
+    float tl[kMaxG];
+    int cnt[kMaxG];
+#pragma unroll
+    for (int hl = 0; hl < kMaxG; ++hl) {
+      tl[hl] = (hl < G) ? misc->t[hl] : INFINITY;
+      cnt[hl] = 0;
+    }
+    for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
+      uint32_t bits = 0;
+      if (i < n) {
+#pragma unroll
+        for (int hsb = 0; hsb < kMaxG / 16; ++hsb) {
+          if (hsb * 16 < SH) {
+            float lv[16];
+            const T* row = sc + (size_t)i * SH + hsb * 16;
+            load8f<T>(row, lv);
+            load8f<T>(row + 8, lv + 8);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const bool pass = lv[k] > tl[hsb * 16 + k];
+              bits |= (uint32_t)pass << (hsb * 16 + k);
+              cnt[hsb * 16 + k] += pass;
+            }
+          }
+        }
+      }
+      hmask[i] = bits;
+    }
+#pragma unroll
+    for (int hl = 0; hl < 16; ++hl) cnt[hl] = warp_sum_i(cnt[hl]);
+    if (SH > 16) {
+#pragma unroll
+      for (int hl = 16; hl < kMaxG; ++hl) cnt[hl] = warp_sum_i(cnt[hl]);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int hl = 0; hl < kMaxG; ++hl)
+        if (hl < G) misc->cntw[warp][hl] = cnt[hl];
+    }
+  }
+}
+
+// Occupancy of one (gather group, 32-position word) task: bit k set if
+// position w*32+k belongs to the group's list. hmask is zero past n.
+template <bool kDense>
+__device__ __forceinline__ uint32_t task_occupancy(const uint32_t* __restrict__ hmask, uint32_t gm, int w, int n) {
+  if constexpr (kDense) {
+    const int rem = n - w * 32;
+    return rem >= 32 ? 0xffffffffu : ((1u << rem) - 1u);
+  } else {
+    const uint4* h4 = reinterpret_cast<const uint4*>(hmask + w * 32);
+    uint32_t occ = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int c = (k + threadIdx.x) & 7;  // rotated so that neighbouring threads hit distinct banks
+      const uint4 v = h4[c];
+      occ |= ((uint32_t)((v.x & gm) != 0u) | ((uint32_t)((v.y & gm) != 0u) << 1) |
+              ((uint32_t)((v.z & gm) != 0u) << 2) | ((uint32_t)((v.w & gm) != 0u) << 3))
+             << (4 * c);
+    }
+    return occ;
+  }
+}
+
+template <typename T, int D, int MODE>
+__device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const T* __restrict__ sc,
+                             const uint32_t* __restrict__ hmask, uint32_t* __restrict__ list, int* __restrict__ toff,
+                             uint32_t* __restrict__ occ, uint8_t* __restrict__ work, uint8_t* __restrict__ wpv,
+                             Misc* misc) {
+  constexpr bool kDense = (MODE == MODE_DENSE);
+  constexpr int ROWB = D * (int)sizeof(T);
+  constexpr int CPR = ROWB / 16;      // 16-byte copies per value row (8, 16 or 32)
+  constexpr int RPI = 32 / CPR;       // rows one warp copies per instruction
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = (n + 31) / 32;
   const int ngroups = misc->ngroups;
   const int ntasks = ngroups * nw;
-  // pass 1: entries per (group, 32-position word)
-  for (int t = warp; t < ntasks; t += kWarps) {
-    const int gi = t / nw, ww = t - gi * nw;
-    const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
-    const uint32_t gm = ((1u << nh) - 1u) << hb;
-    const int pos = ww * 32 + lane;
-    const bool has = pos < n && (kDense || (hmask[pos] & gm) != 0u);
-    const uint32_t bal = __ballot_sync(0xffffffffu, has);
-    if (lane == 0) tcnt[t] = __popc(bal);
-  }
-  __syncthreads();
-  if (warp == 0) {  // exclusive scan in task order
-    int run = 0;
-    for (int b0 = 0; b0 < ntasks; b0 += 32) {
-      const int t = b0 + lane;
-      const int c = t < ntasks ? tcnt[t] : 0;
-      const int incl = warp_incl_scan(c);
-      if (t < ntasks) toff[t] = run + incl - c;
-      run += __shfl_sync(0xffffffffu, incl, 31);
+  // one (gather group, word) task per thread: occupancy, then an exclusive
+  // scan of the counts in task order
+  int carry = 0;
+  for (int t0 = 0; t0 < ntasks; t0 += kThreads) {
+    const int t = t0 + threadIdx.x;
+    int c = 0;
+    if (t < ntasks) {
+      const int gi = t / nw, w = t - gi * nw;
+      const uint32_t o = task_occupancy<kDense>(hmask, misc->gmask[gi], w, n);
+      occ[t] = o;
+      c = __popc(o);
     }
-    if (lane == 0) misc->gstart[ngroups] = run;
+    const int incl = warp_incl_scan(c);
+    if (lane == 31) misc->wsum[warp] = incl;
+    __syncthreads();
+    int wpre = 0, tot = 0;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) {
+      const int ws = misc->wsum[k];
+      wpre += (k < warp) ? ws : 0;
+      tot += ws;
+    }
+    if (t < ntasks) toff[t] = carry + wpre + incl - c;
+    carry += tot;
+    __syncthreads();
+  }
+  // entries in ascending position order within each task
+  for (int t = threadIdx.x; t < ntasks; t += kThreads) {
+    uint32_t o = occ[t];
+    if (!o) continue;
+    const int gi = t / nw, w = t - gi * nw;
+    const uint32_t gm = misc->gmask[gi];
+    const int hb = misc->ghb[gi] & 0xFFFF;
+    int e = toff[t];
+    while (o) {
+      const int bit = __ffs(o) - 1;
+      o &= o - 1u;
+      const int pos = w * 32 + bit;
+      const uint32_t hm = kDense ? gm : (hmask[pos] & gm);
+      list[e++] = (uint32_t)pos | ((hm >> hb) << 16) | ((uint32_t)gi << 24);
+    }
+  }
+  for (int gi = threadIdx.x; gi <= ngroups; gi += kThreads) {
+    misc->gstart[gi] = gi < ngroups ? toff[gi * nw] : carry;
+    if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
+      int s = 0;  // row slots of the groups before gi, each group padded to 16
+      for (int k = 0; k < gi; ++k) {
+        const int e1 = (k + 1 < ngroups) ? toff[(k + 1) * nw] : carry;
+        s += (e1 - toff[k * nw] + 15) & ~15;
+      }
+      misc->gpad[gi] = s;
+    }
   }
   __syncthreads();
-  for (int gi = threadIdx.x; gi < ngroups; gi += kThreads) misc->gstart[gi] = toff[gi * nw];
-  // pass 2: the entries
-  for (int t = warp; t < ntasks; t += kWarps) {
-    const int gi = t / nw, ww = t - gi * nw;
-    const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
-    const uint32_t gm = ((1u << nh) - 1u) << hb;
-    const int pos = ww * 32 + lane;
-    const uint32_t hm = pos < n ? (kDense ? gm : (hmask[pos] & gm)) : 0u;
-    const uint32_t bal = __ballot_sync(0xffffffffu, hm != 0u);
-    if (hm) list[toff[t] + __popc(bal & ((1u << lane) - 1u))] = (uint32_t)pos | ((hm >> hb) << 16) | ((uint32_t)gi << 24);
+  if (threadIdx.x == 0) trace_stamp(p, 5);
+  if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2 && MODE == MODE_AMORTIZED) {
+    // the first pass's weights before its row copies: the copies then do not
+    // hold up these shared-memory reads
+    pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), false);
   }
-  __syncthreads();
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) p.trace[blockIdx.x * 64 + 5] = clock64();
-  const int total = misc->gstart[ngroups];
-  if (total > 0 && total <= p.sm.br) issue_rows<T, D>(p, b, p0, list, 0, total, work, misc);
+  if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
+    if (p.sm.brw > 0) {  // tensor-core P.V: the first pass's rows
+      pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), 0);
+      cp_async_commit();
+    }
+    return;
+  }
+  // value rows, when they all fit one batch: RPI rows per warp instruction,
+  // each row read as CPR consecutive 16-byte segments
+  if (carry > 0 && carry <= p.sm.br) {
+    const int sub = lane / CPR, seg = lane % CPR;
+    const T* vb = reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb + (int64_t)p0 * p.v_sl;
+#pragma unroll 2
+    for (int e = warp * RPI + sub; e < carry; e += kWarps * RPI) {
+      const uint32_t ent = list[e];
+      const T* src = vb + (int64_t)misc->gvh[ent >> 24] * p.v_sh + (int64_t)(ent & 0xFFFFu) * p.v_sl;
+      cp_async16(work + (size_t)e * ROWB + seg * 16, reinterpret_cast<const uint8_t*>(src) + seg * 16, true);
+    }
+  }
+  cp_async_commit();
+}
+
+// Tensor-core P.V of one item (16-bit values, head_dim 128). Per pass of at
+// most brw row slots: rows beyond the first pass are fetched now; the weights
+// (rounded to the value type) go to the K-major operand; the MMA issuer
+// accumulates out^T[d][head slot] += V^T[d][slot] * W[slot][head slot] into 16
+// TMEM columns per gather group. The partial (m, l, o[D]) of every head is
+// then published through the group's tagged slots.
+template <typename T, int D, int MODE>
+__device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0, const T* __restrict__ sc,
+                              const uint32_t* __restrict__ hmask, const uint32_t* __restrict__ list,
+                              uint8_t* __restrict__ work, uint8_t* __restrict__ wpv, Misc* misc, uint32_t tmem_base,
+                              uint32_t& pvph, bool w0_ready) {
+  constexpr bool kDense = (MODE == MODE_DENSE);
+  constexpr uint32_t kIdesc =
+      umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16) | kUmmaAMajorMN;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int G = p.G, SH = p.sh, brw = p.sm.brw;
+  const uint32_t tag = misc->tag;
+  const int ngroups = misc->ngroups;
+  const int TS = misc->gpad[ngroups];
+  const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
+  if (tr) p.trace[blockIdx.x * kTraceCols + 127] = misc->gstart[ngroups];
+  for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) misc->lacc[t] = 0.f;
+  if (brw < 16) {  // unreachable by construction of the layout; no pass could run
+    if (threadIdx.x == 0) set_status(p.status, SAGA_STATUS_WAIT_TIMEOUT);
+    return;
+  }
+  for (int ps0 = 0; ps0 < TS; ps0 += brw) {
+    const int pn = min(brw, TS - ps0);
+    if (ps0 > 0) {
+      pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, ps0, ps0 + pn, ps0);
+      cp_async_commit();
+    }
+    if (!(ps0 == 0 && w0_ready)) pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, ps0, pn, false);
+    cp_async_wait<0>();
+    fence_proxy_async_smem();  // weights and rows -> visible to the tensor cores
+    tc_fence_before();
+    __syncthreads();
+    if (tr && ps0 == 0) trace_stamp(p, 12);
+    if (warp == 1 && lane == 0) {
+      tc_fence_after();
+      for (int ps = 0; ps < pn; ps += 16) {
+        const int gs = ps0 + ps;
+        const int gi = pv_group_of(misc, ngroups, gs);
+        const uint64_t ad = umma_desc_mn_sw128(smem_addr(work + ps * 256), 1024, 2048);
+        const uint64_t bd = umma_desc_sw128(smem_addr(wpv + (ps >> 6) * 2048 + ((ps & 63) >> 4) * 32));
+        umma_f16(tmem_base + (uint32_t)gi * 16u, ad, bd, kIdesc, gs == misc->gpad[gi] ? 0u : 1u);
+      }
+      umma_commit(&misc->pvbar);
+    }
+    // weight sums of the pass from the rounded weights the MMA reads, in a
+    // fixed order (one thread per (group, head), 8 slots per 16-byte load)
+    for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) {
+      const int gi = t >> 3, hh = t & 7;
+      if (hh < (misc->ghb[gi] >> 16)) {
+        const int a = max(misc->gpad[gi], ps0) - ps0, z = min(misc->gpad[gi + 1], ps0 + pn) - ps0;
+        float sum = 0.f;
+        for (int ps = a; ps < z; ps += 8) {
+          const uint4 u = *reinterpret_cast<const uint4*>(wpv + pv_w_off(ps, hh));
+          const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) sum += Num<T>::to_f(e[k]);
+        }
+        misc->lacc[t] += sum;
+      }
+    }
+    mbar_wait(&misc->pvbar, pvph, p.status);  // the pass's rows and weights may now be overwritten
+    pvph ^= 1u;
+    tc_fence_after();
+  }
+  if (tr) trace_stamp(p, 13);
+  // accumulators -> slots: warp w reads TMEM lanes 32 (w % 4) .. + 31 (d),
+  // warps 0-3 the even gather groups, 4-7 the odd ones
+  {
+    const int q = warp & 3;
+    const int d = q * 32 + lane;
+    for (int gi = warp >> 2; gi < ngroups; gi += 2) {
+      const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+      uint32_t r[16];
+      const bool empty = misc->gpad[gi + 1] == misc->gpad[gi];
+      if (!empty) {
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)gi * 16u, r);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) r[k] = 0u;
+      }
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh)
+        if (hh < nh) slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, r[hh]);
+    }
+    tc_fence_before();
+  }
+  for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) {
+    const int gi = t >> 3, hh = t & 7;
+    if (hh < (misc->ghb[gi] >> 16))
+      slot_put(slot_at(p, g, j, (misc->ghb[gi] & 0xFFFF) + hh, kSlotL), tag, __float_as_uint(misc->lacc[t]));
+  }
+  for (int hl = threadIdx.x; hl < G; hl += kThreads)
+    slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
+  if (tr) trace_stamp(p, 14);
 }
 
 template <typename T, int D, int MODE>
@@ -853,13 +1256,13 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
     }
   };
   const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
-  if (tr) p.trace[blockIdx.x * 64 + 63] = total;
+  if (tr) p.trace[blockIdx.x * kTraceCols + 127] = total;
   if (one_batch && total > 0) {
     weights(0, total);
     cp_async_wait<0>();
     __syncthreads();
   }
-  if (tr) p.trace[blockIdx.x * 64 + 12] = clock64();
+  if (tr) trace_stamp(p, 12);
 
   for (int gi = 0; gi < ngroups; ++gi) {
     const int g0 = misc->gstart[gi], g1 = misc->gstart[gi + 1];
@@ -898,7 +1301,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
       }
       if (!one_batch) __syncthreads();
     }
-    if (tr && gi == 0) p.trace[blockIdx.x * 64 + 13] = clock64();
+    if (tr && gi == 0) trace_stamp(p, 13);
     // cross-warp reduction in a fixed order, one head at a time, in the SMEM
     // past the resident rows' weights
     float* red = wbuf + (size_t)BR * 8;  // [kWarps][D + 1]
@@ -923,7 +1326,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
   }
   for (int hl = threadIdx.x; hl < G; hl += kThreads)
     slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
-  if (tr) p.trace[blockIdx.x * 64 + 14] = clock64();
+  if (tr) trace_stamp(p, 14);
 }
 
 // ---------------------------------------------------------------------------
@@ -959,7 +1362,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
       },
       tag, ml, p.status);
   __syncthreads();
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) p.trace[blockIdx.x * 64 + 15] = clock64();
+  if (threadIdx.x == 0) trace_stamp(p, 15);
   float* scl = reinterpret_cast<float*>(ov + nout * C);  // [nhs][C]
   for (int hh = warp; hh < nhs; hh += kWarps) {
     float M = -INFINITY;
@@ -1043,8 +1446,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   uint32_t* eqb = reinterpret_cast<uint32_t*>(smem + p.sm.eq);
   uint32_t* list = reinterpret_cast<uint32_t*>(smem + p.sm.list);
   uint32_t* hmask = reinterpret_cast<uint32_t*>(smem + p.sm.hmask);
-  int* tcnt = reinterpret_cast<int*>(smem + p.sm.sel);  // gather task counts (sel is free by then)
-  int* toff = reinterpret_cast<int*>(smem + p.sm.eq);   // gather task offsets
+  int* toff = reinterpret_cast<int*>(smem + p.sm.sel);       // gather task offsets (sel is free by then)
+  uint32_t* occ = reinterpret_cast<uint32_t*>(smem + p.sm.eq);  // gather task occupancy
   float* wbuf = reinterpret_cast<float*>(smem + p.sm.wbuf);
   uint8_t* work = smem + p.sm.work;
 
@@ -1052,6 +1455,9 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   const int G = p.G, C = p.C, CL = p.CL, SH = p.sh;
   Ring rg;
   uint32_t tmem_base = 0;
+  uint32_t pvph = 0;  // phase of misc->pvbar (every thread waits on every pass)
+  constexpr bool kTcPv = uses_tc_pv(TC, D) && sizeof(T) == 2;
+  uint8_t* wpv = smem + p.sm.wbuf;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
@@ -1062,11 +1468,12 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       mbar_init(&misc->tfull[bb], 1);
       mbar_init(&misc->tempty[bb], 4);
     }
+    mbar_init(&misc->pvbar, 1);
     misc->abort = 0;
     mbar_fence_init();
   }
   if constexpr (TC) {
-    if (warp == 1) tmem_alloc(&misc->tmem_slot, 32);
+    if (warp == 1) tmem_alloc(&misc->tmem_slot, (uint32_t)p.tmem_cols);
     tc_fence_before();
   }
   __syncthreads();
@@ -1076,6 +1483,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   }
 
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
+    if constexpr (TC) tc_fence_after();  // TMEM reads of the previous item precede this item's MMAs
     const int g = item / C, j = item % C;
     const int b = g / p.Hk, kh = g % p.Hk, h0 = kh * G;
     const int p0 = j * CL;
@@ -1087,10 +1495,17 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     const int row0 = b * p.Hq + h0;
     const bool tracing = p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
 #define SAGA_TRACE(k) \
-  if (tracing) p.trace[blockIdx.x * 64 + (k)] = clock64();
+  if (tracing) trace_stamp(p, (k));
     SAGA_TRACE(0)
     if constexpr (MODE != MODE_LOGITS) {  // the logits-only mode has no workspace
-      if (threadIdx.x == 0) misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
+      // a helper warp, so that the TMA producer and the MMA issuer start at once
+      if (warp == 3) {
+        if (lane == 0) {
+          misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
+          plan_gather_groups(p, h0, misc);
+        }
+        if (MODE == MODE_AMORTIZED && lane < G) misc->thr[lane] = p.thr_in[row0 + lane];
+      }
     }
 
     // ---- fused append of the decode token (StaticLayer.update's index_copy_).
@@ -1194,7 +1609,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         float s = 0.f;
         for (int c = 0; c < C; ++c) s += __uint_as_float(xbuf[c * G + hl]);
         s = Num<T>::round(s);
-        const float thr = clamp_min_keep_nan(p.thr_in[row0 + hl], 1e-30f);
+        const float thr = clamp_min_keep_nan(misc->thr[hl], 1e-30f);
         const float t = __fadd_rn(misc->m[hl], logf(__fmul_rn(thr, s)));
         misc->t[hl] = t;
         if (j == 0) {
@@ -1205,42 +1620,9 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       __syncthreads();
       SAGA_TRACE(8)
       // strict selection x > t (triton_atopn.py:42): per position, the mask of
-      // the heads it passes for, and per-thread per-head counts
-      {
-        float tl[kMaxG];
-        int cnt[kMaxG];
-#pragma unroll
-        for (int hl = 0; hl < kMaxG; ++hl) {
-          tl[hl] = (hl < G) ? misc->t[hl] : INFINITY;
-          cnt[hl] = 0;
-        }
-        for (int i = threadIdx.x; i < n; i += kThreads) {
-          uint32_t bits = 0;
-#pragma unroll
-          for (int hsb = 0; hsb < kMaxG / 16; ++hsb) {
-            if (hsb * 16 < G) {
-              float lv[16];
-              const T* row = sc + (size_t)i * SH + hsb * 16;
-              load8f<T>(row, lv);
-              load8f<T>(row + 8, lv + 8);
-#pragma unroll
-              for (int k = 0; k < 16; ++k) {
-                const bool pass = lv[k] > tl[hsb * 16 + k];  // false for padded slots (t = inf)
-                bits |= (uint32_t)pass << (hsb * 16 + k);
-                cnt[hsb * 16 + k] += pass;
-              }
-            }
-          }
-          hmask[i] = bits;
-        }
-#pragma unroll
-        for (int hl = 0; hl < kMaxG; ++hl) {
-          if (hl < G) {
-            const int c = warp_sum_i(cnt[hl]);
-            if (lane == 0) misc->cntw[warp][hl] = c;
-          }
-        }
-      }
+      // the heads it passes for (zero past n up to the word end), and per-head
+      // counts.
+      select_heads<T>(sc, SH, G, n, nw, misc, hmask);
       __syncthreads();
       SAGA_TRACE(9)
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
@@ -1250,8 +1632,9 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         misc->i2[hl] = cnt;
         slot_put(slot_at(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
       }
-      // lists and value-row copies go out while the counts are exchanged
-      gather_begin<T, D, MODE>(p, b, h0, p0, n, hmask, list, tcnt, toff, work, misc);
+      // lists, value-row copies and the first pass's weights go out while the
+      // counts are exchanged
+      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
       slots_gather(C * G, [&](int i) { return slot_at(p, g, i / G, i % G, kSlotCnt); }, tag, xbuf, p.status);
       __syncthreads();
@@ -1315,7 +1698,14 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         }
       }
       SAGA_TRACE(11)
-      gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+      if constexpr (kTcPv) {
+        // heads capped at K changed their bits and stabiliser: redo their weights
+        pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, misc->ngroups, 0,
+                            min(misc->gpad[misc->ngroups], p.sm.brw), true);
+        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, true);
+      }
+      else
+        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else if constexpr (MODE == MODE_CALIBRATE) {
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
@@ -1435,17 +1825,24 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
                                max(0, p.sel_ld - misc->i3[hl]));
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < n; i += kThreads) {
+      for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
         uint32_t bits = 0;
-        for (int hl = 0; hl < G; ++hl) bits |= ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) << hl;
+        if (i < n)
+          for (int hl = 0; hl < G; ++hl) bits |= ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) << hl;
         hmask[i] = bits;
       }
       __syncthreads();
-      gather_begin<T, D, MODE>(p, b, h0, p0, n, hmask, list, tcnt, toff, work, misc);
-      gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      if constexpr (kTcPv)
+        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+      else
+        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
-      gather_begin<T, D, MODE>(p, b, h0, p0, n, hmask, list, tcnt, toff, work, misc);
-      gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      if constexpr (kTcPv)
+        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+      else
+        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     }
     __syncthreads();
 
@@ -1478,7 +1875,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     __syncthreads();
     if (warp == 1) {
       tc_fence_after();
-      tmem_dealloc(tmem_base, 32);
+      tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
     }
   }
 }

@@ -134,11 +134,27 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor, MN-major operand in the 128-byte swizzle
+// layout (16-bit elements): each 128-B row holds 64 consecutive MN elements of
+// one K index; 8 K rows form a 1024-B atom. `lbo` = bytes to the atom of the
+// next 64 MN elements, `sbo` = bytes to the next 8 K rows.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)(lbo >> 4) << 16;
+  d |= (uint64_t)(sbo >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor of kind::f16: fp32 accumulate, A and B of the same
 // 16-bit format (fmt 0 = f16, 1 = bf16), both K-major, M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(uint32_t fmt, uint32_t M, uint32_t N) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
+// Bit of the instruction descriptor that marks A as MN-major.
+constexpr uint32_t kUmmaAMajorMN = 1u << 15;
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {

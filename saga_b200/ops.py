@@ -163,7 +163,7 @@ def _run(fn_name, a, op, device, diag=None):
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     a.status = status_tensor(device).data_ptr()
     if diag is not None and diag.get("trace"):
-        diag["trace"] = torch.zeros((1024, 64), dtype=torch.int64, device=device)
+        diag["trace"] = torch.zeros((1024, 128), dtype=torch.int64, device=device)
         a.trace = diag["trace"].data_ptr()
     rc = getattr(L.lib, fn_name)(ctypes.byref(a), _stream(device))
     L.check(rc, fn_name)
