@@ -22,6 +22,7 @@ namespace {
 struct DevInfo {
   int sms = 0;
   int smem_optin = 0;
+  int smem_per_sm = 0;
 };
 
 DevInfo dev_info() {
@@ -32,6 +33,7 @@ DevInfo dev_info() {
   if (dev != cached_dev) {
     cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&info.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&info.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cached_dev = dev;
   }
   return info;
@@ -147,16 +149,36 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   pl->nvh = ngg;
   pl->tc = tc;
   pl->cooperative = (mode != MODE_LOGITS);
+  // TMEM columns per CTA: the scorer's two 16-column accumulators, or output
+  // and weight sums (2 x 16 columns) per gather group for the tensor-core P.V
+  pl->tmem_cols = 32;
+  if (uses_tc_pv(tc, a->D)) {
+    // up to 4 16-column accumulators per gather group, within 256 columns
+    const int want = 16 * ngg * std::max(1, std::min(4, 256 / (16 * ngg)));
+    while (pl->tmem_cols < want) pl->tmem_cols *= 2;  // ngg <= 16 on this path: at most 256
+  }
   const void* kfn = pick_kernel(a->dtype, a->D, mode, tc, a->mask != nullptr);
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm.total) != cudaSuccess) {
+  // The CTAs on one SM must fit its 512 TMEM columns together (an allocation
+  // that does not fit would wait): ask for enough shared memory that no more
+  // of them share an SM.
+  const int max_per_sm = tc ? std::max(1, 512 / pl->tmem_cols) : 1 << 30;
+  if (tc && di.smem_per_sm > 0) {
+    const int floor_smem = di.smem_per_sm / (max_per_sm + 1) + 1024;
+    if (pl->smem < floor_smem) pl->smem = std::min(floor_smem, budget);
+  }
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, pl->smem) != cudaSuccess) {
     *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(cudaGetLastError());
     return SAGA_ERR_CUDA;
   }
   int nb = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kfn, kThreads, sm.total) != cudaSuccess || nb <= 0) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kfn, kThreads, pl->smem) != cudaSuccess || nb <= 0) {
     *err = "occupancy query failed";
     cudaGetLastError();
     return SAGA_ERR_CUDA;
+  }
+  if (nb > max_per_sm) {
+    *err = "cannot bound the CTAs per SM to the TMEM columns they need";
+    return SAGA_ERR_UNSUPPORTED;
   }
   const int cap = nb * di.sms;
   if (pl->cooperative && C > cap) {
@@ -188,9 +210,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   p.G = pl.G; p.Gv = pl.Gv;
   p.C = pl.C; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
   p.sh = pl.G <= 16 ? 16 : 32;
-  p.tmem_cols = 32;
-  if (uses_tc_pv(pl.tc, a->D))
-    while (p.tmem_cols < 16 * pl.nvh) p.tmem_cols *= 2;  // nvh <= 16 on this path: at most 256
+  p.tmem_cols = pl.tmem_cols;
   p.tail = std::min(kTail, a->L);
   if (mode == MODE_AMORTIZED) p.buf_k = std::min(2 * a->top_n, a->L);
   else if (mode == MODE_CALIBRATE) p.buf_k = std::min(a->top_n, a->L);

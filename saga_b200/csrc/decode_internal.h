@@ -102,7 +102,7 @@ struct DecodeParams {
   CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
   int B, Hq, Hk, Hv, D, L, G, Gv;
   int C, CL, items, tail, buf_k, ns, nvh, sh;
-  int tmem_cols;  // TMEM columns per CTA: the scorer's 2 x 16, or 16 per gather group for the P.V
+  int tmem_cols;  // TMEM columns per CTA: the scorer's 2 x 16, or up to 4 x 16 per gather group for the P.V
   const void* q; int64_t q_sb, q_sh;
   const void* k; int64_t k_sb, k_sh, k_sl;
   const void* v; int64_t v_sb, v_sh, v_sl;
@@ -123,7 +123,7 @@ struct DecodeParams {
 };
 
 struct DecodePlan {
-  int G, Gv, groups, C, CL, items, grid, smem, ns, nvh;
+  int G, Gv, groups, C, CL, items, grid, smem, ns, nvh, tmem_cols;
   bool cooperative, tc;
   size_t ws_ctrl, ws_stats, ws_part, ws_hist, ws_total;
 };

@@ -108,6 +108,14 @@ __device__ __forceinline__ void trace_stamp(const DecodeParams& p, int k) {
   }
 }
 
+// Sub-phase stamp k < 40 of the optional trace (SM clock, column 80 + k),
+// written by thread 0 of CTA c < 1024 (its last item wins): where a phase
+// spends its time. Columns 120-122 hold the global timer at kernel entry,
+// after the set-up and at exit.
+__device__ __forceinline__ void trace_sub(const DecodeParams& p, int k) {
+  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) p.trace[blockIdx.x * kTraceCols + 80 + k] = clock64();
+}
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src),
                "r"(valid ? 16 : 0)
@@ -801,9 +809,9 @@ __device__ __forceinline__ void issue_rows(const DecodeParams& p, int b, int p0,
 //  * value rows: row slot s, 16-byte segment sg (8 elements) -> byte offset
 //    in the MN-major 128-B swizzle layout: 8-slot groups of two 1024-B atoms
 //    (elements 0-63 and 64-127 of the row), the segment index XOR-ed with s % 8;
-//  * weights: slot s, head slot n (16 per gather group, the unused ones zero)
-//    -> byte offset in the K-major 128-B swizzle layout: blocks of 64 slots x
-//    16 head slots, one 128-B row per head slot.
+//  * weights: slot s, head slot n < 16 -> byte offset in the K-major 128-B
+//    swizzle layout: blocks of 64 slots x 16 head slots, one 128-B row per
+//    head slot (only the group's heads are read back; see pv_weights).
 __device__ __forceinline__ int pv_row_off(int s, int sg) {
   return (s >> 3) * 2048 + (sg >> 3) * 1024 + (s & 7) * 128 + (((sg & 7) ^ (s & 7)) << 4);
 }
@@ -847,9 +855,12 @@ __device__ __forceinline__ void pv_issue_rows(const DecodeParams& p, int b, int 
 }
 
 // Weights of the P.V operand for pass slots [0, pn) (global slots ps0 + ...):
-// one task per (8-slot chunk, head slot) computes 8 weights and stores them as
-// one 16-byte K-major segment. Head slots past the group's heads, padding
-// slots and unselected (row, head) pairs get 0. With `capped_only`, only the
+// one task per (8-slot chunk, head slot < 8) computes 8 weights and stores
+// them as one 16-byte K-major segment; padding slots and unselected (row,
+// head) pairs get 0. Only the MMA output columns of real heads are read, so
+// head slots past the group's heads are left as they are, and the second half
+// of each 64-slot block (head slots 8-15) holds the 8-weight partial sums:
+// float at block + 1024 + chunk * 32 + head * 4. With `capped_only`, only the
 // heads whose chunk was capped at K (keep < passing) are recomputed.
 template <typename T, int MODE>
 __device__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
@@ -857,17 +868,19 @@ __device__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, cons
                            int ngroups, int ps0, int pn, bool capped_only) {
   constexpr bool kDense = (MODE == MODE_DENSE);
   const int SH = p.sh;
-  for (int i = threadIdx.x; i < (pn >> 3) * 16; i += kThreads) {
-    const int c8 = i >> 4, nn = i & 15;
+  for (int i = threadIdx.x; i < (pn >> 3) * 8; i += kThreads) {
+    const int c8 = i >> 3, nn = i & 7;
     const int ps = c8 * 8, gs = ps0 + ps;
     const int gi = pv_group_of(misc, ngroups, gs);
     const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
     const int hl = hb + nn;
-    if (capped_only && (nn >= nh || misc->i1[hl] >= misc->i2[hl])) continue;
+    if (nn >= nh) continue;
+    if (capped_only && misc->i1[hl] >= misc->i2[hl]) continue;
     const int e0 = misc->gstart[gi], rows = misc->gstart[gi + 1] - e0;
     const int r0 = gs - misc->gpad[gi];
     uint4 u = make_uint4(0u, 0u, 0u, 0u);
-    if (nn < nh && r0 < rows) {
+    float psum = 0.f;
+    if (r0 < rows) {
       // all loads first (indices clamped to a real row), so the 8 chains overlap
       int pos[8];
       uint32_t hm[8];
@@ -881,13 +894,17 @@ __device__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, cons
 #pragma unroll
       for (int k = 0; k < 8; ++k) l[k] = Num<T>::to_f(sc[pos[k] * SH + hl]);
       T* e = reinterpret_cast<T*>(&u);
+      float wr[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const bool on = (r0 + k < rows) && (kDense || ((hm[k] >> hl) & 1u));
         e[k] = Num<T>::from_f(on ? weight_from_logit<T, MODE>(l[k], misc, hl) : 0.f);
+        wr[k] = Num<T>::to_f(e[k]);  // the rounded weight the MMA multiplies
       }
+      psum = ((wr[0] + wr[1]) + (wr[2] + wr[3])) + ((wr[4] + wr[5]) + (wr[6] + wr[7]));
     }
     *reinterpret_cast<uint4*>(wpv + pv_w_off(ps, nn)) = u;
+    *reinterpret_cast<float*>(wpv + (ps >> 6) * 2048 + 1024 + ((ps & 63) >> 3) * 32 + nn * 4) = psum;
   }
 }
 
@@ -1047,6 +1064,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
   // one (gather group, word) task per thread: occupancy, then an exclusive
   // scan of the counts in task order
   int carry = 0;
+  trace_sub(p, 0);
   for (int t0 = 0; t0 < ntasks; t0 += kThreads) {
     const int t = t0 + threadIdx.x;
     int c = 0;
@@ -1056,9 +1074,11 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
       occ[t] = o;
       c = __popc(o);
     }
+    trace_sub(p, 1);
     const int incl = warp_incl_scan(c);
     if (lane == 31) misc->wsum[warp] = incl;
     __syncthreads();
+    trace_sub(p, 2);
     int wpre = 0, tot = 0;
 #pragma unroll
     for (int k = 0; k < kWarps; ++k) {
@@ -1070,6 +1090,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
     carry += tot;
     __syncthreads();
   }
+  trace_sub(p, 3);
   // entries in ascending position order within each task
   for (int t = threadIdx.x; t < ntasks; t += kThreads) {
     uint32_t o = occ[t];
@@ -1086,6 +1107,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
       list[e++] = (uint32_t)pos | ((hm >> hb) << 16) | ((uint32_t)gi << 24);
     }
   }
+  trace_sub(p, 4);
   for (int gi = threadIdx.x; gi <= ngroups; gi += kThreads) {
     misc->gstart[gi] = gi < ngroups ? toff[gi * nw] : carry;
     if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
@@ -1103,11 +1125,13 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
     // the first pass's weights before its row copies: the copies then do not
     // hold up these shared-memory reads
     pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), false);
+    trace_sub(p, 5);
   }
   if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
     if (p.sm.brw > 0) {  // tensor-core P.V: the first pass's rows
       pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), 0);
       cp_async_commit();
+      trace_sub(p, 6);
     }
     return;
   }
@@ -1138,13 +1162,14 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
                               uint8_t* __restrict__ work, uint8_t* __restrict__ wpv, Misc* misc, uint32_t tmem_base,
                               uint32_t& pvph, bool w0_ready) {
   constexpr bool kDense = (MODE == MODE_DENSE);
-  constexpr uint32_t kIdesc =
-      umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16) | kUmmaAMajorMN;
+  constexpr uint32_t kIdesc = umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16) | kUmmaAMajorMN;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int G = p.G, SH = p.sh, brw = p.sm.brw;
   const uint32_t tag = misc->tag;
   const int ngroups = misc->ngroups;
   const int TS = misc->gpad[ngroups];
+  // accumulators per gather group: as many as the TMEM columns allow, at most 4
+  const int nch = min(4, p.tmem_cols / (16 * max(ngroups, 1)));
   const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
   if (tr) p.trace[blockIdx.x * kTraceCols + 127] = misc->gstart[ngroups];
   for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) misc->lacc[t] = 0.f;
@@ -1159,39 +1184,58 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
       cp_async_commit();
     }
     if (!(ps0 == 0 && w0_ready)) pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, ps0, pn, false);
+    if (ps0 == 0) trace_sub(p, 10);
     cp_async_wait<0>();
+    if (ps0 == 0) trace_sub(p, 11);
     fence_proxy_async_smem();  // weights and rows -> visible to the tensor cores
     tc_fence_before();
     __syncthreads();
     if (tr && ps0 == 0) trace_stamp(p, 12);
     if (warp == 1 && lane == 0) {
       tc_fence_after();
-      for (int ps = 0; ps < pn; ps += 16) {
-        const int gs = ps0 + ps;
-        const int gi = pv_group_of(misc, ngroups, gs);
-        const uint64_t ad = umma_desc_mn_sw128(smem_addr(work + ps * 256), 1024, 2048);
-        const uint64_t bd = umma_desc_sw128(smem_addr(wpv + (ps >> 6) * 2048 + ((ps & 63) >> 4) * 32));
-        umma_f16(tmem_base + (uint32_t)gi * 16u, ad, bd, kIdesc, gs == misc->gpad[gi] ? 0u : 1u);
+      const uint64_t ad0 = umma_desc_mn_sw128(smem_addr(work), 1024, 2048);
+      const uint64_t bd0 = umma_desc_sw128(smem_addr(wpv));
+      for (int gi = 0; gi < ngroups; ++gi) {
+        const int a = max(misc->gpad[gi], ps0), z = min(misc->gpad[gi + 1], ps0 + pn);
+        const uint32_t tcol = tmem_base + (uint32_t)(gi * nch) * 16u;
+        // K steps go round-robin to nch independent accumulators. Descriptor
+        // start addresses are in 16-byte units: a K step is 4096 B of rows;
+        // 32 B of weights within a 64-slot block, 2048 B per block.
+        int ks = (a - misc->gpad[gi]) >> 4, c = ks % nch;
+        for (int ps = a - ps0; ps < z - ps0; ps += 16, ++ks) {
+          const uint64_t ad = ad0 + (uint64_t)(ps * 16);
+          const uint64_t bd = bd0 + (uint64_t)((ps >> 6) * 128 + ((ps & 63) >> 4) * 2);
+          umma_f16(tcol + (uint32_t)c * 16u, ad, bd, kIdesc, ks < nch ? 0u : 1u);
+          c = (c + 1 == nch) ? 0 : c + 1;
+        }
       }
       umma_commit(&misc->pvbar);
+      if (p.trace && blockIdx.x < 1024 && ps0 == 0) p.trace[blockIdx.x * kTraceCols + 80 + 14] = clock64();
     }
-    // weight sums of the pass from the rounded weights the MMA reads, in a
-    // fixed order (one thread per (group, head), 8 slots per 16-byte load)
+    // weight sums of the pass: the 8-slot partials of each (group, head) in
+    // slot order
     for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) {
       const int gi = t >> 3, hh = t & 7;
       if (hh < (misc->ghb[gi] >> 16)) {
         const int a = max(misc->gpad[gi], ps0) - ps0, z = min(misc->gpad[gi + 1], ps0 + pn) - ps0;
-        float sum = 0.f;
-        for (int ps = a; ps < z; ps += 8) {
-          const uint4 u = *reinterpret_cast<const uint4*>(wpv + pv_w_off(ps, hh));
-          const T* e = reinterpret_cast<const T*>(&u);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) sum += Num<T>::to_f(e[k]);
+        auto part = [&](int ps) {
+          return *reinterpret_cast<const float*>(wpv + (ps >> 6) * 2048 + 1024 + ((ps & 63) >> 3) * 32 + hh * 4);
+        };
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // independent chains, combined in a fixed order
+        int ps = a;
+        for (; ps + 24 < z; ps += 32) {
+          s0 += part(ps);
+          s1 += part(ps + 8);
+          s2 += part(ps + 16);
+          s3 += part(ps + 24);
         }
-        misc->lacc[t] += sum;
+        for (; ps < z; ps += 8) s0 += part(ps);
+        misc->lacc[t] += (s0 + s1) + (s2 + s3);
       }
     }
+    if (ps0 == 0) trace_sub(p, 12);
     mbar_wait(&misc->pvbar, pvph, p.status);  // the pass's rows and weights may now be overwritten
+    if (ps0 == 0) trace_sub(p, 13);
     pvph ^= 1u;
     tc_fence_after();
   }
@@ -1203,17 +1247,20 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
     const int d = q * 32 + lane;
     for (int gi = warp >> 2; gi < ngroups; gi += 2) {
       const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
-      uint32_t r[16];
-      const bool empty = misc->gpad[gi + 1] == misc->gpad[gi];
-      if (!empty) {
-        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)gi * 16u, r);
-      } else {
+      // accumulators that received at least one K step
+      const int used = min(nch, (misc->gpad[gi + 1] - misc->gpad[gi]) >> 4);
+      float o[8];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) r[k] = 0u;
+      for (int hh = 0; hh < 8; ++hh) o[hh] = 0.f;
+      for (int c = 0; c < used; ++c) {  // fixed order: run-to-run identical sums
+        uint32_t r[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((gi * nch + c) * 16), r);
+#pragma unroll
+        for (int hh = 0; hh < 8; ++hh) o[hh] += __uint_as_float(r[hh]);
       }
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh)
-        if (hh < nh) slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, r[hh]);
+        if (hh < nh) slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(o[hh]));
     }
     tc_fence_before();
   }
@@ -1364,6 +1411,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
   __syncthreads();
   if (threadIdx.x == 0) trace_stamp(p, 15);
   float* scl = reinterpret_cast<float*>(ov + nout * C);  // [nhs][C]
+  trace_sub(p, 20);
   for (int hh = warp; hh < nhs; hh += kWarps) {
     float M = -INFINITY;
     for (int c = lane; c < C; c += 32) M = nanmax(M, __uint_as_float(ml[(hh * C + c) * 2]));
@@ -1380,6 +1428,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
     if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(Ls, 1e-12f) : Ls;
   }
   __syncthreads();
+  trace_sub(p, 21);
   for (int k = threadIdx.x; k < nout; k += kThreads) {
     const int o = lo + k;
     const int hh = o / D - hl0, d = o % D;
@@ -1459,6 +1508,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   constexpr bool kTcPv = uses_tc_pv(TC, D) && sizeof(T) == 2;
   uint8_t* wpv = smem + p.sm.wbuf;
 
+  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
+    p.trace[blockIdx.x * kTraceCols + 120] = (long long)globaltimer_ns();
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&misc->full[s], 1);
@@ -1482,6 +1533,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     tmem_base = misc->tmem_slot;
   }
 
+  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
+    p.trace[blockIdx.x * kTraceCols + 121] = (long long)globaltimer_ns();
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     if constexpr (TC) tc_fence_after();  // TMEM reads of the previous item precede this item's MMAs
     const int g = item / C, j = item % C;
@@ -1878,6 +1931,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
     }
   }
+  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
+    p.trace[blockIdx.x * kTraceCols + 122] = (long long)globaltimer_ns();
 }
 
 
