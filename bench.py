@@ -64,6 +64,20 @@ def parse():
 # helpers
 # ---------------------------------------------------------------------------
 
+def ncu_traffic(workload: str, mode: str):
+    """DRAM bytes (read + write) of one launch of the timed kernel, from the
+    committed ncu summary of this workload (profiles/), or None."""
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                        f"saga_decode_kernel_{'amortized' if mode == 'atopn' else mode}_{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("| traffic (read + write) per launch |"):
+                return int(float(line.split("|")[2].split()[0]) * 1e6)
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
 def measured_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -358,7 +372,7 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_8TBs_nominal": round(achieved / 8000.0, 4),
-                "traffic": None, "algorithmic_bytes_per_step": abytes,
+                "traffic": ncu_traffic(args.workload, args.mode), "algorithmic_bytes_per_step": abytes,
                 "kernel": "saga_decode_kernel<amortized>" if args.mode == "atopn" else f"saga_decode_kernel<{args.mode}>"}
     if rank == 0:
         line = {"metric": metric, "value": round(B * world / (ms * 1e-3), 1), "unit": unit, "n_gpus": world,

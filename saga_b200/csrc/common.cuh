@@ -172,6 +172,45 @@ __device__ __forceinline__ int warp_incl_scan(int v) {
   return v;
 }
 
+// Reduces v[0..15] with `op` across the 32 lanes of the warp by halving the
+// live values at each butterfly step (15 shuffles instead of 16 x 5). Lanes
+// 2k and 2k + 1 return the reduction of value k. The combination order is
+// fixed, so sums are identical from run to run.
+template <typename V, typename Op>
+__device__ __forceinline__ V warp_reduce16(const V (&v)[16], Op op) {
+  const int lane = threadIdx.x & 31;
+  V a[8], b[4], c[2];
+  bool up = (lane & 16) != 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const V send = up ? v[k] : v[k + 8];
+    a[k] = op(up ? v[k + 8] : v[k], __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+  up = (lane & 8) != 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const V send = up ? a[k] : a[k + 4];
+    b[k] = op(up ? a[k + 4] : a[k], __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  up = (lane & 4) != 0;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const V send = up ? b[k] : b[k + 2];
+    c[k] = op(up ? b[k + 2] : b[k], __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  up = (lane & 2) != 0;
+  V d = op(up ? c[1] : c[0], __shfl_xor_sync(0xffffffffu, up ? c[0] : c[1], 2));
+  return op(d, __shfl_xor_sync(0xffffffffu, d, 1));
+}
+
+// Division by a runtime divisor d >= 1 through a 64-bit reciprocal: exact for
+// x * d < 2^32 (q = floor(x * ceil(2^32 / d) / 2^32)).
+struct FastDiv {
+  uint64_t m;
+  __device__ __forceinline__ explicit FastDiv(uint32_t d) : m(((1ull << 32) + d - 1) / d) {}
+  __device__ __forceinline__ uint32_t div(uint32_t x) const { return (uint32_t)((x * m) >> 32); }
+};
+
 // NaN-propagating max (torch.max semantics): NaN wins.
 __device__ __forceinline__ float nanmax(float a, float b) {
   return (a != a || b != b) ? __int_as_float(0x7fffffff) : fmaxf(a, b);

@@ -177,30 +177,32 @@ __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* 
   return v;
 }
 // All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i].
-// Each thread keeps up to 8 loads in flight and re-polls all of its pending
-// slots together, so a late publisher costs one round trip, not one per slot.
-// Bounded: after kWaitLimitNs the status word gets SAGA_STATUS_WAIT_TIMEOUT
-// and the stale values are used.
+// Each thread keeps up to 8 loads in flight (addresses computed once) and
+// re-polls all of its pending slots together, so a late publisher costs one
+// round trip, not one per slot. Bounded: after kWaitLimitNs the status word
+// gets SAGA_STATUS_WAIT_TIMEOUT and the stale values are used.
 template <typename AddrFn>
 __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t tag, uint32_t* dst, int* status) {
   for (int base = threadIdx.x; base < count; base += kThreads * 8) {
+    const unsigned long long* a[8];
     unsigned long long v[8];
     uint32_t pending = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int i = base + k * kThreads;
-      v[k] = (i < count) ? slot_ld(addr(i)) : 0ull;
+      a[k] = (i < count) ? addr(i) : nullptr;
       if (i < count) pending |= 1u << k;
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = ((pending >> k) & 1u) ? slot_ld(a[k]) : 0ull;
     unsigned long long t0 = 0;
+#pragma unroll 1
     for (uint32_t it = 1;; ++it) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        if ((pending >> k) & 1u) {
-          if ((uint32_t)(v[k] >> 32) == tag) {
-            dst[base + k * kThreads] = (uint32_t)v[k];
-            pending &= ~(1u << k);
-          }
+        if (((pending >> k) & 1u) && (uint32_t)(v[k] >> 32) == tag) {
+          dst[base + k * kThreads] = (uint32_t)v[k];
+          pending &= ~(1u << k);
         }
       }
       if (!pending) break;
@@ -219,7 +221,7 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
       __nanosleep(32);
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if ((pending >> k) & 1u) v[k] = slot_ld(addr(base + k * kThreads));
+        if ((pending >> k) & 1u) v[k] = slot_ld(a[k]);
     }
   }
 }
@@ -547,10 +549,9 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       if (pre && q == n_pre - 1) {
         // tail max of the group: warp max, then the last of the four epilogue
         // warps combines and publishes it (helpers and epilogue both wait)
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float v = warp_nanmax(tm[k]);
-          if (lane == 0) misc->tmax4[q4][k] = v;
+        {
+          const float v = warp_reduce16(tm, [](float x, float y) { return nanmax(x, y); });
+          if ((lane & 1) == 0) misc->tmax4[q4][lane >> 1] = v;
         }
         __syncwarp();
         if (lane == 0) {
@@ -586,16 +587,12 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
     }
     if (MODE == MODE_AMORTIZED) {
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        if (k < 2 * EJ) {
-          const float sv = warp_sum(es[k]);
-          const float mv = warp_max(em[k]);
-          if (lane == 0) {
-            misc->esum4[q4][k] = sv;
-            misc->emax4[q4][k] = mv;
-          }
-        }
+      const float sv = warp_reduce16(es, [](float x, float y) { return x + y; });
+      const float mv = warp_reduce16(em, [](float x, float y) { return fmaxf(x, y); });
+      const int k = lane >> 1;
+      if ((lane & 1) == 0 && k < 2 * EJ) {
+        misc->esum4[q4][k] = sv;
+        misc->emax4[q4][k] = mv;
       }
     }
   } else if (warp == 2 || warp == 3) {
@@ -687,15 +684,13 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         }
       }
     }
-#pragma unroll
-    for (int hl = 0; hl < 16; ++hl) {
-      if (hl < G) {
-        const float sv = warp_sum(s[hl]);
-        const float mv = warp_max(mx[hl]);
-        if (lane == 0) {
-          misc->ered[hw][hl] = sv;
-          misc->emax[hw][hl] = mv;
-        }
+    {
+      const float sv = warp_reduce16(s, [](float x, float y) { return x + y; });
+      const float mv = warp_reduce16(mx, [](float x, float y) { return fmaxf(x, y); });
+      const int hl = lane >> 1;
+      if ((lane & 1) == 0 && hl < G) {
+        misc->ered[hw][hl] = sv;
+        misc->emax[hw][hl] = mv;
       }
     }
   }
@@ -829,7 +824,7 @@ __device__ __forceinline__ int pv_group_of(const Misc* misc, int ngroups, int s)
 // s - pbase: rows of real entries from the cache, padding slots zero-filled.
 // RPI = 2 rows per warp instruction, 16 segments each.
 template <typename T>
-__device__ __forceinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0, const uint32_t* __restrict__ list,
+__device__ __noinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0, const uint32_t* __restrict__ list,
                                               uint8_t* __restrict__ work, const Misc* misc, int ngroups, int s0,
                                               int s1, int pbase) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -863,7 +858,7 @@ __device__ __forceinline__ void pv_issue_rows(const DecodeParams& p, int b, int 
 // float at block + 1024 + chunk * 32 + head * 4. With `capped_only`, only the
 // heads whose chunk was capped at K (keep < passing) are recomputed.
 template <typename T, int MODE>
-__device__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
+__device__ __noinline__ void pv_weights(const DecodeParams& p, const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
                            const uint32_t* __restrict__ list, uint8_t* __restrict__ wpv, const Misc* misc,
                            int ngroups, int ps0, int pn, bool capped_only) {
   constexpr bool kDense = (MODE == MODE_DENSE);
@@ -970,17 +965,12 @@ __device__ __forceinline__ void select_heads(const T* __restrict__ sc, int SH, i
       }
       hmask[i] = bits;
     }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) c2[k] = (uint32_t)warp_sum_i((int)c2[k]);
-    if (npairs > 8) {
-#pragma unroll
-      for (int k = 8; k < 16; ++k) c2[k] = (uint32_t)warp_sum_i((int)c2[k]);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        if (2 * k < G) misc->cntw[warp][2 * k] = (int)(c2[k] & 0xFFFFu);
-        if (2 * k + 1 < G) misc->cntw[warp][2 * k + 1] = (int)(c2[k] >> 16);
+    {
+      const uint32_t c = warp_reduce16(c2, [](uint32_t x, uint32_t y) { return x + y; });
+      const int k = lane >> 1;  // head pair of this lane
+      if ((lane & 1) == 0) {
+        if (2 * k < G) misc->cntw[warp][2 * k] = (int)(c & 0xFFFFu);
+        if (2 * k + 1 < G) misc->cntw[warp][2 * k + 1] = (int)(c >> 16);
       }
     }
   } else {
@@ -1012,16 +1002,21 @@ __device__ __forceinline__ void select_heads(const T* __restrict__ sc, int SH, i
       }
       hmask[i] = bits;
     }
+    {
+      int lo[16], hi[16];
 #pragma unroll
-    for (int hl = 0; hl < 16; ++hl) cnt[hl] = warp_sum_i(cnt[hl]);
-    if (SH > 16) {
-#pragma unroll
-      for (int hl = 16; hl < kMaxG; ++hl) cnt[hl] = warp_sum_i(cnt[hl]);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int hl = 0; hl < kMaxG; ++hl)
-        if (hl < G) misc->cntw[warp][hl] = cnt[hl];
+      for (int k = 0; k < 16; ++k) {
+        lo[k] = cnt[k];
+        hi[k] = cnt[16 + k];
+      }
+      const auto add = [](int x, int y) { return x + y; };
+      const int cl = warp_reduce16(lo, add);
+      const int ch = (SH > 16) ? warp_reduce16(hi, add) : 0;
+      const int k = lane >> 1;
+      if ((lane & 1) == 0) {
+        if (k < G) misc->cntw[warp][k] = cl;
+        if (16 + k < G) misc->cntw[warp][16 + k] = ch;
+      }
     }
   }
 }
@@ -1396,16 +1391,26 @@ __device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, 
   uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][C][2]
   uint32_t* ov = ml + nhs * C * 2;                      // [nout][C]
   const int n_ml = nhs * C * 2;
+  const FastDiv div2c((uint32_t)(2 * C)), divc((uint32_t)C);
+  const unsigned long long* s0 = slot_at(p, g, 0, 0, 0);
   slots_gather(
       n_ml + nout * C,
       [&](int i) {
+        int c, hl, f;
         if (i < n_ml) {
-          const int hh = i / (2 * C), r = i % (2 * C);
-          return slot_at(p, g, r >> 1, hl0 + hh, kSlotM + (r & 1));
+          const int hh = (int)div2c.div((uint32_t)i), r = i - hh * 2 * C;
+          c = r >> 1;
+          hl = hl0 + hh;
+          f = kSlotM + (r & 1);
+        } else {
+          const int k = i - n_ml;
+          const int kq = (int)divc.div((uint32_t)k);
+          const int o = lo + kq;
+          c = k - kq * C;
+          hl = o / D;
+          f = kSlotO + o % D;
         }
-        const int k = i - n_ml;
-        const int o = lo + k / C, c = k % C;
-        return slot_at(p, g, c, o / D, kSlotO + o % D);
+        return s0 + ((size_t)c * G + hl) * (D + 4) + f;
       },
       tag, ml, p.status);
   __syncthreads();
@@ -1654,7 +1659,10 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // exchange the partial exp-sums (attention.py:145: sum over the row)
       for (int hl = threadIdx.x; hl < G; hl += kThreads)
         slot_put(slot_at(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
-      slots_gather(C * G, [&](int i) { return slot_at(p, g, i / G, i % G, kSlotS); }, tag, xbuf, p.status);
+      {  // slot (chunk c, head hl) sits at index c * G + hl of the group's slots
+        const unsigned long long* s0 = slot_at(p, g, 0, 0, kSlotS);
+        slots_gather(C * G, [&](int i) { return s0 + (size_t)i * (D + 4); }, tag, xbuf, p.status);
+      }
       __syncthreads();
       SAGA_TRACE(2)
       // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
@@ -1689,7 +1697,10 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // counts are exchanged
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
-      slots_gather(C * G, [&](int i) { return slot_at(p, g, i / G, i % G, kSlotCnt); }, tag, xbuf, p.status);
+      {
+        const unsigned long long* s0 = slot_at(p, g, 0, 0, kSlotCnt);
+        slots_gather(C * G, [&](int i) { return s0 + (size_t)i * (D + 4); }, tag, xbuf, p.status);
+      }
       __syncthreads();
       SAGA_TRACE(4)
       // exclusive prefix in chunk order: keep the K lowest passing positions
