@@ -64,6 +64,28 @@ def parse():
 # helpers
 # ---------------------------------------------------------------------------
 
+# ---------------------------------------------------------------------------
+# multi-GPU host logic: replicas, one per rank, each on its own batch
+# ---------------------------------------------------------------------------
+
+def replica_seed(rank: int, copy: int) -> int:
+    """Seed of a rank's input copy: every rank decodes its own batch."""
+    return 1000 * rank + copy
+
+
+def max_over_ranks(torch, dist, value: float, device, world: int) -> float:
+    """The slowest rank's time: every rank takes part, in the same order."""
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(batch_per_rank: int, world: int, ms_per_step: float) -> float:
+    """Whole-job tokens/s: all ranks' sequences per step over the slowest rank's step time."""
+    return batch_per_rank * world / (ms_per_step * 1e-3)
+
+
 def ncu_traffic(workload: str, mode: str):
     """DRAM bytes (read + write) of one launch of the timed kernel, from the
     committed ncu summary of this workload (profiles/), or None."""
@@ -249,7 +271,7 @@ def main():
             dist.barrier()
 
     copies = 4 if (B * Hk * L * D * 2) < 2 * L2_BYTES else 1
-    caches = [make_device_inputs(torch, shape, dev, seed=1000 * rank + c) for c in range(copies)]
+    caches = [make_device_inputs(torch, shape, dev, seed=replica_seed(rank, c)) for c in range(copies)]
     q1 = caches[0][1]
     thrs = []
     for c in range(copies):
@@ -319,11 +341,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / steps_timed
-    tmax = torch.tensor([ms], device=dev)
-    if world > 1:
-        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-    ms = float(tmax.item())
+    ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / steps_timed, dev, world)
     status = ops.read_status(dev)
 
     # end to end through the public API with host buffers
@@ -361,10 +379,7 @@ def main():
     f1.record()
     torch.cuda.synchronize()
     barrier()
-    ms_e2e = torch.tensor([f0.elapsed_time(f1) / ne], device=dev)
-    if world > 1:
-        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
-    ms_e2e = float(ms_e2e.item())
+    ms_e2e = max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
 
     peak, peak_kind = measured_peaks()
     abytes = algorithmic_bytes(shape, union, args.mode)
@@ -375,12 +390,12 @@ def main():
                 "traffic": ncu_traffic(args.workload, args.mode), "algorithmic_bytes_per_step": abytes,
                 "kernel": "saga_decode_kernel<amortized>" if args.mode == "atopn" else f"saga_decode_kernel<{args.mode}>"}
     if rank == 0:
-        line = {"metric": metric, "value": round(B * world / (ms * 1e-3), 1), "unit": unit, "n_gpus": world,
+        line = {"metric": metric, "value": round(job_throughput(B, world, ms), 1), "unit": unit, "n_gpus": world,
                 "steps": steps_timed, "warmup": args.warmup, "ms_per_step": round(ms, 5),
                 "us_per_layer_step": round(ms * 1e3, 3),
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic", "config": config,
-                "e2e": {"value": round(B * world / (ms_e2e * 1e-3), 1), "unit": unit, "h2d_bytes_per_step": h2d,
+                "e2e": {"value": round(job_throughput(B, world, ms_e2e), 1), "unit": unit, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 5)},
                 "roofline": roofline, "clocks": clocks,
                 "gpu_launches": steps_timed * launches_per_step,

@@ -99,21 +99,29 @@ struct Ring {
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
 };
 
-// Phase stamp k < 16 of the optional trace: SM clock at column k, global
-// timer (ns, comparable across SMs) at column 64 + k.
-__device__ __forceinline__ void trace_stamp(const DecodeParams& p, int k) {
-  if (p.trace && blockIdx.x < 1024) {
-    p.trace[blockIdx.x * kTraceCols + k] = clock64();
-    p.trace[blockIdx.x * kTraceCols + 64 + k] = (long long)globaltimer_ns();
-  }
+// Optional phase trace (diagnostics). The stores are out of line, so that a
+// stamp site costs one test of p.trace when tracing is off.
+//  * trace_stamp(k), k < 16: SM clock at column k, global timer (ns,
+//    comparable across SMs) at column 64 + k;
+//  * trace_sub(k), k < 40: SM clock at column 80 + k, written by thread 0 of
+//    CTA c < 1024 (its last item wins): where a phase spends its time;
+//  * trace_col(col, v): raw value (columns 16-63 tile stamps, 120-122 global
+//    timer at kernel entry, after set-up and at exit, 127 rows gathered).
+static __device__ __noinline__ void trace_write(long long* trace, int col, long long v) {
+  trace[blockIdx.x * kTraceCols + col] = v;
 }
-
-// Sub-phase stamp k < 40 of the optional trace (SM clock, column 80 + k),
-// written by thread 0 of CTA c < 1024 (its last item wins): where a phase
-// spends its time. Columns 120-122 hold the global timer at kernel entry,
-// after the set-up and at exit.
+static __device__ __noinline__ void trace_stamp_now(long long* trace, int k) {
+  trace[blockIdx.x * kTraceCols + k] = clock64();
+  trace[blockIdx.x * kTraceCols + 64 + k] = (long long)globaltimer_ns();
+}
+__device__ __forceinline__ void trace_stamp(const DecodeParams& p, int k) {
+  if (p.trace && blockIdx.x < 1024) trace_stamp_now(p.trace, k);
+}
 __device__ __forceinline__ void trace_sub(const DecodeParams& p, int k) {
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) p.trace[blockIdx.x * kTraceCols + 80 + k] = clock64();
+  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) trace_write(p.trace, 80 + k, clock64());
+}
+__device__ __forceinline__ void trace_col(const DecodeParams& p, int col, long long v) {
+  if (p.trace && blockIdx.x < 1024) trace_write(p.trace, col, v);
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -224,6 +232,13 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
         if ((pending >> k) & 1u) v[k] = slot_ld(a[k]);
     }
   }
+}
+
+// slots_gather over `count` consecutive slots: base + i * stride. One out-of-
+// line copy serves every exchange of per-(chunk, head) scalars.
+static __device__ __noinline__ void slots_gather_linear(const unsigned long long* base, int stride, int count,
+                                                        uint32_t tag, uint32_t* dst, int* status) {
+  slots_gather(count, [&](int i) { return base + (size_t)i * stride; }, tag, dst, status);
 }
 
 // The reference's rounding chain for one logit (attention.py:121-126).
@@ -396,7 +411,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         for (int kb = 0; kb < KB; ++kb)
           tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
         ++issued;
-        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * kTraceCols + 16 + q] = clock64();
+        if (q < 16) trace_col(p, 16 + q, clock64());
         if (++rg.ps == (uint32_t)NS) {
           rg.ps = 0;
           rg.pph ^= 1u;
@@ -441,7 +456,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         last_b = rg.mb;
         last_ph = rg.mbph;
         ++issued;
-        if (p.trace && blockIdx.x < 1024 && q < 16) p.trace[blockIdx.x * kTraceCols + 32 + q] = clock64();
+        if (q < 16) trace_col(p, 32 + q, clock64());
         if (++rg.ms == (uint32_t)NS) {
           rg.ms = 0;
           rg.mph ^= 1u;
@@ -540,8 +555,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         }
       }
       __syncwarp();
-      if (!pre && p.trace && blockIdx.x < 1024 && q - n_pre < 16 && q4 == 0 && lane == 0)
-        p.trace[blockIdx.x * kTraceCols + 48 + (q - n_pre)] = clock64();
+      if (!pre && q - n_pre < 16 && q4 == 0 && lane == 0) trace_col(p, 48 + (q - n_pre), clock64());
       if (!pre && lane == 0) {
         __threadfence_block();
         atomicAdd(&misc->stored, 1);
@@ -1166,7 +1180,7 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
   // accumulators per gather group: as many as the TMEM columns allow, at most 4
   const int nch = min(4, p.tmem_cols / (16 * max(ngroups, 1)));
   const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
-  if (tr) p.trace[blockIdx.x * kTraceCols + 127] = misc->gstart[ngroups];
+  if (tr) trace_col(p, 127, misc->gstart[ngroups]);
   for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) misc->lacc[t] = 0.f;
   if (brw < 16) {  // unreachable by construction of the layout; no pass could run
     if (threadIdx.x == 0) set_status(p.status, SAGA_STATUS_WAIT_TIMEOUT);
@@ -1205,7 +1219,7 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
         }
       }
       umma_commit(&misc->pvbar);
-      if (p.trace && blockIdx.x < 1024 && ps0 == 0) p.trace[blockIdx.x * kTraceCols + 80 + 14] = clock64();
+      if (ps0 == 0) trace_col(p, 80 + 14, clock64());
     }
     // weight sums of the pass: the 8-slot partials of each (group, head) in
     // slot order
@@ -1298,7 +1312,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
     }
   };
   const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
-  if (tr) p.trace[blockIdx.x * kTraceCols + 127] = total;
+  if (tr) trace_col(p, 127, total);
   if (one_batch && total > 0) {
     weights(0, total);
     cp_async_wait<0>();
@@ -1513,8 +1527,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   constexpr bool kTcPv = uses_tc_pv(TC, D) && sizeof(T) == 2;
   uint8_t* wpv = smem + p.sm.wbuf;
 
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
-    p.trace[blockIdx.x * kTraceCols + 120] = (long long)globaltimer_ns();
+  if (threadIdx.x == 0) trace_col(p, 120, (long long)globaltimer_ns());
   if (threadIdx.x == 0) {
     for (int s = 0; s < kMaxStages; ++s) {
       mbar_init(&misc->full[s], 1);
@@ -1538,8 +1551,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     tmem_base = misc->tmem_slot;
   }
 
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
-    p.trace[blockIdx.x * kTraceCols + 121] = (long long)globaltimer_ns();
+  if (threadIdx.x == 0) trace_col(p, 121, (long long)globaltimer_ns());
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     if constexpr (TC) tc_fence_after();  // TMEM reads of the previous item precede this item's MMAs
     const int g = item / C, j = item % C;
@@ -1659,10 +1671,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // exchange the partial exp-sums (attention.py:145: sum over the row)
       for (int hl = threadIdx.x; hl < G; hl += kThreads)
         slot_put(slot_at(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
-      {  // slot (chunk c, head hl) sits at index c * G + hl of the group's slots
-        const unsigned long long* s0 = slot_at(p, g, 0, 0, kSlotS);
-        slots_gather(C * G, [&](int i) { return s0 + (size_t)i * (D + 4); }, tag, xbuf, p.status);
-      }
+      // slot (chunk c, head hl) sits at index c * G + hl of the group's slots
+      slots_gather_linear(slot_at(p, g, 0, 0, kSlotS), D + 4, C * G, tag, xbuf, p.status);
       __syncthreads();
       SAGA_TRACE(2)
       // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
@@ -1697,10 +1707,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // counts are exchanged
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
-      {
-        const unsigned long long* s0 = slot_at(p, g, 0, 0, kSlotCnt);
-        slots_gather(C * G, [&](int i) { return s0 + (size_t)i * (D + 4); }, tag, xbuf, p.status);
-      }
+      slots_gather_linear(slot_at(p, g, 0, 0, kSlotCnt), D + 4, C * G, tag, xbuf, p.status);
       __syncthreads();
       SAGA_TRACE(4)
       // exclusive prefix in chunk order: keep the K lowest passing positions
@@ -1942,8 +1949,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
     }
   }
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024)
-    p.trace[blockIdx.x * kTraceCols + 122] = (long long)globaltimer_ns();
+  if (threadIdx.x == 0) trace_col(p, 122, (long long)globaltimer_ns());
 }
 
 
