@@ -40,6 +40,8 @@ WORKLOADS = {
     # name: (B, L, Hq, Hk, Hv, D, N, plant)
     "config2": (8, 32768, 12, 1, 2, 128, 512, 64),
     "config4": (1, 131072, 12, 1, 2, 128, 1024, 256),
+    # the same model with its unmerged key heads, for the dense-GQA baseline (--mode dense)
+    "config2_gqa": (8, 32768, 12, 2, 2, 128, 512, 64),
     "config3_layer": (16, 16384 + 128, 15, 1, 5, 64, 256, 64),
     "config5_layer": (64, 65536 + 64, 12, 1, 4, 128, 512, 128),
 }
@@ -241,6 +243,8 @@ def main():
               "parallelism": f"replicas x{world} (batch-sharded, no collective)",
               "l2": "rotating KV-cache copies, each step reads a cache not in L2"}
     metric = "decode tokens/s of one Atop-N attention layer (config 2 shapes)"
+    if args.mode != "atopn" or args.workload != "config2":
+        metric = f"decode tokens/s of one attention layer, {args.mode} ({args.workload} shapes)"
     unit = "tokens/s"
 
     if args.impl == "reference":
