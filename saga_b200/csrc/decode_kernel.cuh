@@ -91,6 +91,14 @@ struct Misc {
 };
 static_assert(sizeof(Misc) <= 6144, "Misc must fit its 6 KB slot");
 
+template <int MODE>
+__device__ __forceinline__ void item_prologue(const DecodeParams& p, int b, int kh, Misc* misc);
+
+// Head pairs whose exp-sums the 4 epilogue warps fold while scoring (the 2
+// helper warps take the rest): two thirds, which keeps both roles within one
+// tile period (each helper warp covers twice the positions of an epilogue warp).
+__device__ __forceinline__ int epilogue_exp_pairs(int G) { return (2 * ((G + 1) / 2) + 2) / 3; }
+
 // Per-thread pipeline positions kept across items (only role threads use theirs).
 struct Ring {
   uint32_t ps = 0, pph = 0;   // producer stage / phase
@@ -378,6 +386,30 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
   const int nseq = n_pre + ntl;
   const int tail_start = p.L - p.tail;
 
+  // The ring's stages are free at item start: the producer sends the first
+  // tiles before the B operand is staged (the caller's barrier already made
+  // the appended key row visible to TMA).
+  int pre_issued = 0;
+  if (warp == 0 && lane == 0) {
+    for (int q = 0; q < min(NS, nseq); ++q) {
+      if (!mbar_wait(&misc->empty[rg.ps], rg.pph ^ 1u, p.status)) {
+        misc->abort = 1;
+        break;
+      }
+      const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
+      mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
+      uint8_t* dst = ring + rg.ps * TILE_BYTES;
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
+      if (q < 16) trace_col(p, 16 + q, clock64());
+      ++pre_issued;
+      if (++rg.ps == (uint32_t)NS) {
+        rg.ps = 0;
+        rg.pph ^= 1u;
+      }
+    }
+  }
   // B operand: query heads of the group as 16 rows x D, swizzled.
   for (int i = threadIdx.x; i < 16 * (D / 8); i += kThreads) {
     const int h = i / (D / 8), c8 = i % (D / 8);
@@ -398,8 +430,8 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int q = 0; q < nseq && !misc->abort; ++q) {
+      int issued = pre_issued;
+      for (int q = pre_issued; q < nseq && !misc->abort; ++q) {
         if (!mbar_wait(&misc->empty[rg.ps], rg.pph ^ 1u, p.status)) {
           misc->abort = 1;
           break;
@@ -468,6 +500,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
       // all UMMAs of this item complete before their operands are reused
       if (issued) mbar_wait(&misc->tfull[last_b], last_ph, p.status);
+      trace_col(p, 80 + 35, clock64());  // last tile's MMAs complete
     }
   } else if (warp >= 4) {
     // epilogue: TMEM -> logits (reference rounding chain) -> SMEM, 32 B per
@@ -475,7 +508,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     // tiles into per-head exp-sums and maxima (the helpers take the rest)
     const int q4 = warp - 4;  // TMEM lane quarter of this warp
     const float scl = p.scaling;
-    const int EJ = (MODE == MODE_AMORTIZED) ? ((G + 1) / 2) / 2 : 0;
+    const int EJ = (MODE == MODE_AMORTIZED) ? epilogue_exp_pairs(G) : 0;
     float es[16], em[16], tm[16];
     P2 m2[8];
 #pragma unroll
@@ -600,6 +633,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
           if (jj < EJ) m2[jj] = PT::pack_rn(misc->m[2 * jj], misc->m[2 * jj + 1]);
       }
     }
+    if (q4 == 0 && lane == 0) trace_col(p, 80 + 31, clock64());  // epilogue done with the tiles
     if (MODE == MODE_AMORTIZED) {
       const float sv = warp_reduce16(es, [](float x, float y) { return x + y; });
       const float mv = warp_reduce16(em, [](float x, float y) { return fmaxf(x, y); });
@@ -610,9 +644,13 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
     }
   } else if (warp == 2 || warp == 3) {
-    // helpers: tail max first (each helper warp over all tail positions), then
-    // the per-head exp-sum and maximum of every stored own tile
+    // helpers: the item's exchange tag, gather groups and thresholds (their
+    // global loads wait here, not in front of the scorer), then the per-head
+    // exp-sum and maximum of every stored own tile
     const int hw = warp - 2;
+    if constexpr (MODE != MODE_LOGITS) {
+      if (warp == 3) item_prologue<MODE>(p, b, kh, misc);
+    }
     float m[16], s[16], mx[16];
 #pragma unroll
     for (int hl = 0; hl < 16; ++hl) {
@@ -663,7 +701,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
 #pragma unroll
       for (int hl = 0; hl < 16; ++hl) m[hl] = misc->m[hl];
     }
-    const int EJ = (MODE == MODE_AMORTIZED) ? ((G + 1) / 2) / 2 : 0;
+    const int EJ = (MODE == MODE_AMORTIZED) ? epilogue_exp_pairs(G) : 0;
     P2 m2[8];
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) m2[jj] = PT::pack_rn(m[2 * jj], m[2 * jj + 1]);
@@ -698,6 +736,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         }
       }
     }
+    if (lane == 0) trace_col(p, 80 + 32 + hw, clock64());  // helper warp done with the tiles
     {
       const float sv = warp_reduce16(s, [](float x, float y) { return x + y; });
       const float mv = warp_reduce16(mx, [](float x, float y) { return fmaxf(x, y); });
@@ -915,6 +954,22 @@ __device__ __noinline__ void pv_weights(const DecodeParams& p, const T* __restri
     *reinterpret_cast<uint4*>(wpv + pv_w_off(ps, nn)) = u;
     *reinterpret_cast<float*>(wpv + (ps >> 6) * 2048 + 1024 + ((ps & 63) >> 3) * 32 + nn * 4) = psum;
   }
+}
+
+__device__ __forceinline__ void plan_gather_groups(const DecodeParams& p, int h0, Misc* misc);
+
+// Per-item set-up done by one warp (the logits-only mode has no workspace):
+// the exchange tag of this launch, the gather groups, and for amortized the
+// rows' softmax-space thresholds.
+template <int MODE>
+__device__ __forceinline__ void item_prologue(const DecodeParams& p, int b, int kh, Misc* misc) {
+  const int lane = threadIdx.x & 31;
+  const int G = p.G, h0 = kh * G;
+  if (lane == 0) {
+    misc->tag = (uint32_t)ld_acquire_gpu(p.ctrl + (size_t)(b * p.Hk + kh) * kCtrlInts) + 1u;
+    plan_gather_groups(p, h0, misc);
+  }
+  if (MODE == MODE_AMORTIZED && lane < G) misc->thr[lane] = p.thr_in[b * p.Hq + h0 + lane];
 }
 
 // Gather groups of an item: (value head, <= 8 of its query heads in this key
@@ -1567,15 +1622,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 #define SAGA_TRACE(k) \
   if (tracing) trace_stamp(p, (k));
     SAGA_TRACE(0)
-    if constexpr (MODE != MODE_LOGITS) {  // the logits-only mode has no workspace
-      // a helper warp, so that the TMA producer and the MMA issuer start at once
-      if (warp == 3) {
-        if (lane == 0) {
-          misc->tag = (uint32_t)ld_acquire_gpu(ctrl) + 1u;
-          plan_gather_groups(p, h0, misc);
-        }
-        if (MODE == MODE_AMORTIZED && lane < G) misc->thr[lane] = p.thr_in[row0 + lane];
-      }
+    if constexpr (MODE != MODE_LOGITS && !TC) {  // the tensor-core scorer does it in a helper warp
+      if (warp == 3) item_prologue<MODE>(p, b, kh, misc);
     }
 
     // ---- fused append of the decode token (StaticLayer.update's index_copy_).
@@ -1612,7 +1660,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       __syncthreads();
       score_chunk_tc<T, D, MODE, MASK>(p, b, kh, p0, n, pre0, n_pre, sc, tsc, qop, work, misc, rg, tmem_base);
-      const int ej2 = (MODE == MODE_AMORTIZED) ? 2 * (((G + 1) / 2) / 2) : 0;
+      const int ej2 = (MODE == MODE_AMORTIZED) ? 2 * epilogue_exp_pairs(G) : 0;
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         if (hl < ej2) {  // heads folded by the epilogue warps
           misc->s[hl] = ((misc->esum4[0][hl] + misc->esum4[1][hl]) + misc->esum4[2][hl]) + misc->esum4[3][hl];
