@@ -237,10 +237,15 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    # config 4 runs one long sequence sharded over the ranks (strong scaling);
+    # the other workloads run one replica per rank (weak scaling)
+    sharded = args.workload == "config4" and world > 1 and args.mode in ("atopn", "dense")
     config = {"workload": f"{args.workload}: one SAGA attention layer, batch {B}, context {L}, "
                           f"Hq {Hq} / Hk {Hk} / Hv {Hv}, head_dim {D}, N {N}, mode {args.mode}",
               "batch_per_gpu": B, "seq_len": L, "heads": [Hq, Hk, Hv], "head_dim": D, "top_n": N,
-              "parallelism": f"replicas x{world} (batch-sharded, no collective)",
+              "parallelism": (f"sequence-sharded x{world} (one fused launch per device; exchanges through "
+                              f"peer-mapped workspaces over NVLink, no collective on the data path)") if sharded
+              else f"replicas x{world} (batch-sharded, no collective)",
               "l2": "rotating KV-cache copies, each step reads a cache not in L2"}
     metric = "decode tokens/s of one Atop-N attention layer (config 2 shapes)"
     if args.mode != "atopn" or args.workload != "config2":
@@ -275,7 +280,8 @@ def main():
             dist.barrier()
 
     copies = 4 if (B * Hk * L * D * 2) < 2 * L2_BYTES else 1
-    caches = [make_device_inputs(torch, shape, dev, seed=replica_seed(rank, c)) for c in range(copies)]
+    caches = [make_device_inputs(torch, shape, dev, seed=c if sharded else replica_seed(rank, c))
+              for c in range(copies)]
     q1 = caches[0][1]
     thrs = []
     for c in range(copies):
@@ -303,8 +309,18 @@ def main():
     launches_per_step = len(diag["launches"])
     ops.read_status(dev)
 
+    sd = None
+    if sharded:
+        from saga_b200.seqpar import ShardedDecode, shard_cache
+        sd = ShardedDecode(dist.group.WORLD, dev, B, L, Hq, Hk, Hv, D, op=args.mode)
+        # keep only this rank's shard (+ tail replica) of every cache copy
+        caches = [(c[0], c[1], shard_cache(c[2], sd.lay), shard_cache(c[3], sd.lay), c[4], c[5]) for c in caches]
+        torch.cuda.synchronize()
+
     def step(i, q):
         _, _, kc, vc, kn, vn = caches[i % copies]
+        if sd is not None:
+            return sd(q, kc, vc, thrs[i % copies], N, k_new=kn, v_new=vn, append_pos=L - 1)
         if args.mode == "atopn":
             return ops.atopn_decode(q, kc, vc, None, thrs[i % copies], N, k_new=kn, v_new=vn, append_pos=L - 1)
         if args.mode == "dense":
@@ -329,10 +345,18 @@ def main():
     sampler = ClockSampler(gpu_id, enabled=not args.no_clocks)
     sampler.start()
     with torch.cuda.stream(stream):
-        t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < 0.5:   # untimed soak so the clocks settle
-            graph.replay()
+        if sharded:
+            # the shards of a step run together: every rank replays the same
+            # number of steps (a rank with an extra launch would wait for a
+            # partner launch that never comes)
+            for _ in range(max(1, 2000 // copies)):
+                graph.replay()
             stream.synchronize()
+        else:
+            t_soak = time.perf_counter()
+            while time.perf_counter() - t_soak < 0.5:   # untimed soak so the clocks settle
+                graph.replay()
+                stream.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
@@ -363,7 +387,9 @@ def main():
         qd = hq.to(dev, non_blocking=True)
         knd = hkn.to(dev, non_blocking=True)
         vnd = hvn.to(dev, non_blocking=True)
-        if args.mode == "atopn":
+        if sd is not None:
+            o = sd(qd, kc, vc, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
+        elif args.mode == "atopn":
             o = ops.atopn_decode(qd, kc, vc, None, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
         elif args.mode == "dense":
             o = ops.dense_decode(qd, kc, vc, None, k_new=knd, v_new=vnd, append_pos=L - 1)
@@ -385,21 +411,27 @@ def main():
     barrier()
     ms_e2e = max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
 
+    if sd is not None:  # unmap the peers' workspaces once every rank is done with them
+        barrier()
+        sd.close()
+        barrier()
     peak, peak_kind = measured_peaks()
     abytes = algorithmic_bytes(shape, union, args.mode)
-    achieved = abytes / (ms * 1e-3) / 1e9
+    # per device: a sharded step spreads the job's bytes over the ranks
+    achieved = abytes / (world if sharded else 1) / (ms * 1e-3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "frac_of_8TBs_nominal": round(achieved / 8000.0, 4),
                 "traffic": ncu_traffic(args.workload, args.mode), "algorithmic_bytes_per_step": abytes,
                 "kernel": "saga_decode_kernel<amortized>" if args.mode == "atopn" else f"saga_decode_kernel<{args.mode}>"}
     if rank == 0:
-        line = {"metric": metric, "value": round(job_throughput(B, world, ms), 1), "unit": unit, "n_gpus": world,
+        ranks_b = 1 if sharded else world  # a sharded job decodes one batch per step over all ranks
+        line = {"metric": metric, "value": round(job_throughput(B, ranks_b, ms), 1), "unit": unit, "n_gpus": world,
                 "steps": steps_timed, "warmup": args.warmup, "ms_per_step": round(ms, 5),
                 "us_per_layer_step": round(ms * 1e3, 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": config,
-                "e2e": {"value": round(job_throughput(B, world, ms_e2e), 1), "unit": unit, "h2d_bytes_per_step": h2d,
+                "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic", "config": config,
+                "e2e": {"value": round(job_throughput(B, ranks_b, ms_e2e), 1), "unit": unit, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 5)},
                 "roofline": roofline, "clocks": clocks,
                 "gpu_launches": steps_timed * launches_per_step,

@@ -104,6 +104,24 @@ typedef struct SagaAttnArgs {
    * (< 16) was issued by TMA / multiplied / stored; 127 = value rows
    * gathered. Diagnostics only. */
   int64_t* trace;
+
+  /* Sequence sharding (config 4 of the reference's benchmarks): the positions
+   * of every group are split over `shards` devices, one call per device, all
+   * in flight together. This call owns positions [0, nsel) of its caches, which
+   * are global positions pos_offset + [0, nsel); when nsel < L, positions
+   * [nsel, L) are a replica of the sequence's last kTail (256) rows, used
+   * only for the tail max (attention.py:142-143). The exchanges of the fused
+   * kernel (exp-sums, counts, partial outputs, completion) run between the
+   * devices through their workspaces: shard_workspaces[s] is shard s's
+   * workspace mapped into this device (peer memory over NVLink), and
+   * shard_workspaces[shard] == workspace. All shards must use the same
+   * shapes and nsel. Every shard writes the full output. Supported for
+   * saga_atopn_decode and saga_dense_decode. shards = 0 or 1: not sharded. */
+  int32_t nsel;        /* 0 = L */
+  int32_t pos_offset;  /* added to the positions written to sel_idx_out */
+  int32_t shards;
+  int32_t shard;
+  void* shard_workspaces[8];
 } SagaAttnArgs;
 
 /* Ops understood by saga_workspace_bytes. */
@@ -193,6 +211,18 @@ SAGA_API int saga_kv_append(int32_t dtype, int32_t B, int32_t Hk, int32_t Hv, in
                    int64_t v_sb, int64_t v_sh, int64_t v_sl, const void* k_new, int64_t kn_sb,
                    int64_t kn_sh, const void* v_new, int64_t vn_sb, int64_t vn_sh,
                    void* stream);
+
+/* Set-up helpers of sequence sharding (no counterpart in the reference).
+ * saga_ipc_handle writes the 64-byte cudaIpcMemHandle of the device
+ * allocation that contains `ptr` and the byte offset of `ptr` in it (the
+ * allocation must come from cudaMalloc, as torch's caching allocator does by
+ * default). saga_ipc_open maps another process's allocation into the CURRENT
+ * device with peer access enabled, so that kernels on this device read and
+ * write it over NVLink; *ptr receives the allocation's base (add the offset).
+ * saga_ipc_close unmaps it. */
+SAGA_API int saga_ipc_handle(const void* ptr, void* handle64, size_t* offset);
+SAGA_API int saga_ipc_open(const void* handle64, void** ptr);
+SAGA_API int saga_ipc_close(void* ptr);
 
 /* Message of the last error on the calling thread ("" if none). */
 SAGA_API const char* saga_last_error(void);

@@ -41,6 +41,8 @@ class SagaAttnArgs(ctypes.Structure):
         ("workspace", _vp), ("workspace_bytes", _sz),
         ("status", _vp),
         ("trace", _vp),
+        ("nsel", _i32), ("pos_offset", _i32), ("shards", _i32), ("shard", _i32),
+        ("shard_workspaces", _vp * 8),
     ]
 
 
@@ -59,6 +61,9 @@ SIGNATURES = {
                                   _i32, _vp, _i64, _i64, _vp]),
     "saga_kv_append": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _i64, _i64, _i64, _vp, _i64, _i64,
                               _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp]),
+    "saga_ipc_handle": (_i32, [_vp, _vp, ctypes.POINTER(_sz)]),
+    "saga_ipc_open": (_i32, [_vp, ctypes.POINTER(_vp)]),
+    "saga_ipc_close": (_i32, [_vp]),
     "saga_last_error": (ctypes.c_char_p, []),
     "saga_version": (ctypes.c_char_p, []),
     "saga_last_launches": (ctypes.c_char_p, []),

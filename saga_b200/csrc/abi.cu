@@ -1,7 +1,9 @@
 // extern "C" entry points of libsaga_b200.so: argument validation, then the
 // launchers. Invalid requests are rejected on the host so that no kernel is
 // ever launched on arguments it cannot handle.
+#include <cuda.h>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 #include "../../include/saga_b200.h"
@@ -63,6 +65,21 @@ int check_attn(const SagaAttnArgs* a, int op) {
     if (op == SAGA_OP_ATOPN_DECODE && !a->thr_in) return fail(SAGA_ERR_INVALID, "thr_in required");
   }
   if (a->sel_idx_out && a->sel_ld <= 0) return fail(SAGA_ERR_INVALID, "sel_ld must be positive");
+  if (a->nsel < 0 || a->nsel > a->L) return fail(SAGA_ERR_INVALID, "nsel outside [0, L]");
+  if (a->nsel > 0 && a->nsel < a->L && a->L - a->nsel != 256)
+    return fail(SAGA_ERR_INVALID, "positions past nsel must be exactly the 256-row tail replica");
+  if (a->shards > 1) {
+    if (a->shards > 8 || a->shard < 0 || a->shard >= a->shards)
+      return fail(SAGA_ERR_INVALID, "shards in [1, 8] and 0 <= shard < shards required");
+    if (op != SAGA_OP_ATOPN_DECODE && op != SAGA_OP_DENSE_DECODE)
+      return fail(SAGA_ERR_UNSUPPORTED, "sequence sharding supports the decode and dense ops");
+    if (a->dtype == SAGA_FP32 || a->Hq / a->Hk > 16)
+      return fail(SAGA_ERR_UNSUPPORTED, "sequence sharding needs the tensor-core path (16-bit, G <= 16)");
+    for (int s = 0; s < a->shards; ++s)
+      if (!a->shard_workspaces[s]) return fail(SAGA_ERR_INVALID, "every shard workspace must be mapped");
+    if (a->shard_workspaces[a->shard] != a->workspace)
+      return fail(SAGA_ERR_INVALID, "shard_workspaces[shard] must be this call's workspace");
+  }
   if (a->k_new || a->v_new) {
     if (!a->k_new || !a->v_new) return fail(SAGA_ERR_INVALID, "k_new and v_new go together");
     if (a->append_pos < 0 || a->append_pos >= a->L) return fail(SAGA_ERR_INVALID, "append_pos outside [0, L)");
@@ -183,6 +200,51 @@ int saga_gather_output(int32_t dtype, const void* w, const int64_t* idx, int32_t
                                o_sb, o_sh, reinterpret_cast<cudaStream_t>(stream), &err);
   if (rc) return fail(rc, err);
   g_launched = "gather_kernel";
+  return SAGA_OK;
+}
+
+int saga_ipc_handle(const void* ptr, void* handle64, size_t* offset) {
+  g_err.clear();
+  if (!ptr || !handle64 || !offset) return fail(SAGA_ERR_INVALID, "NULL argument");
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (!get_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return fail(SAGA_ERR_CUDA, "cuMemGetAddressRange unavailable");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(SAGA_ERR_INVALID, "pointer is not device memory");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail(SAGA_ERR_CUDA, std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
+  memcpy(handle64, &h, sizeof(h));
+  *offset = reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base);
+  return SAGA_OK;
+}
+
+int saga_ipc_open(const void* handle64, void** ptr) {
+  g_err.clear();
+  if (!handle64 || !ptr) return fail(SAGA_ERR_INVALID, "NULL handle or pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(SAGA_ERR_CUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+  *ptr = p;
+  return SAGA_OK;
+}
+
+int saga_ipc_close(void* ptr) {
+  g_err.clear();
+  if (!ptr) return SAGA_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(SAGA_ERR_CUDA, std::string("cudaIpcCloseMemHandle: ") + cudaGetErrorString(e));
   return SAGA_OK;
 }
 

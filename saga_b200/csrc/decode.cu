@@ -97,13 +97,17 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   }
   const int G = a->Hq / a->Hk, Gv = a->Hq / a->Hv;
   const int groups = a->B * a->Hk;
-  const int ntiles = (a->L + kTile - 1) / kTile;
+  const int nsel = (a->nsel > 0) ? a->nsel : a->L;  // this call's own positions
+  const int ntiles = (nsel + kTile - 1) / kTile;
   const int es = esize_of(a->dtype);
   const bool tc = (a->dtype != SAGA_FP32) && G <= 16;
   const int ngg = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
   // tensor-core path: one CTA per SM, deepest K ring that fits; else two per SM
   const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
-  const int cbound = std::min(ntiles, 4096);
+  // the exchanges stage every chunk of the group: with sequence sharding,
+  // the other devices' chunks too
+  const int shards = a->shards > 1 ? a->shards : 1;
+  const int cbound = std::min(ntiles, 4096) * shards;
   const int target = tc ? di.sms : 2 * di.sms;
   const int c_par = std::max(1, target / std::max(1, groups));
   // Deepest K ring whose chunk still lets every group run in one wave; if no
@@ -111,7 +115,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   auto tiles_for = [&](int stages) {
     int mt = 0;
     for (int t = 1; t <= ntiles; ++t) {
-      if (smem_layout(G, a->D, t * kTile, es, cbound, tc, stages, ngg).total <= budget) mt = t;
+      if (smem_layout(G, a->D, t * kTile, es, cbound, std::max(1, cbound / shards), tc, stages, ngg).total <= budget) mt = t;
       else break;
     }
     return mt;
@@ -136,7 +140,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   int tiles = (ntiles + C - 1) / C;
   C = (ntiles + tiles - 1) / tiles;
   const int CL = tiles * kTile;
-  const SmemLayout sm = smem_layout(G, a->D, CL, es, C, tc, ns, ngg);
+  const SmemLayout sm = smem_layout(G, a->D, CL, es, C * shards, C, tc, ns, ngg);
 
   pl->G = G;
   pl->Gv = Gv;
@@ -191,7 +195,9 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   pl->ws_hist = al256((size_t)groups * kCtrlInts * 4);
   pl->ws_stats = pl->ws_hist + (mode == MODE_CALIBRATE ? al256((size_t)groups * 4 * G * 256 * 4) : 0);
   pl->ws_part = pl->ws_stats + (mode == MODE_CALIBRATE ? al256((size_t)groups * C * G * sizeof(ChunkStat)) : 0);
-  pl->ws_total = pl->ws_part + al256((size_t)groups * C * G * (a->D + 4) * 8);
+  // chunk slots, then (sequence sharding) the device's combined values
+  pl->ws_total = pl->ws_part + al256((size_t)groups * C * G * (a->D + 4) * 8) +
+                 (shards > 1 ? al256((size_t)groups * G * (a->D + 4) * 8) : 0);
   return SAGA_OK;
 }
 
@@ -208,7 +214,13 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   memset(&p, 0, sizeof(p));
   p.B = a->B; p.Hq = a->Hq; p.Hk = a->Hk; p.Hv = a->Hv; p.D = a->D; p.L = a->L;
   p.G = pl.G; p.Gv = pl.Gv;
-  p.C = pl.C; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
+  const int shards = a->shards > 1 ? a->shards : 1;
+  p.C = pl.C * shards; p.CL = pl.CL; p.items = pl.items; p.ns = pl.ns; p.nvh = pl.nvh;
+  p.c_local = pl.C;
+  p.shards = shards;
+  p.shard = shards > 1 ? a->shard : 0;
+  p.nsel = (a->nsel > 0) ? a->nsel : a->L;
+  p.pos_offset = a->pos_offset;
   p.sh = pl.G <= 16 ? 16 : 32;
   p.tmem_cols = pl.tmem_cols;
   p.tail = std::min(kTail, a->L);
@@ -234,10 +246,21 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     p.hist = mode == MODE_CALIBRATE ? reinterpret_cast<int*>(ws + pl.ws_hist) : nullptr;
     p.stats = mode == MODE_CALIBRATE ? reinterpret_cast<ChunkStat*>(ws + pl.ws_stats) : nullptr;
     p.slots = reinterpret_cast<unsigned long long*>(ws + pl.ws_part);
+    p.ctrl_home = p.ctrl;
+    p.slot_base[0] = p.slots;
+    p.ctrl_peer[0] = p.ctrl;
+    if (shards > 1) {  // every shard's workspace has the same layout
+      for (int s2 = 0; s2 < shards; ++s2) {
+        uint8_t* w = reinterpret_cast<uint8_t*>(a->shard_workspaces[s2]);
+        p.slot_base[s2] = reinterpret_cast<unsigned long long*>(w + pl.ws_part);
+        p.ctrl_peer[s2] = reinterpret_cast<int*>(w + pl.ws_ctrl);
+      }
+      p.ctrl_home = p.ctrl_peer[0];
+    }
   }
   p.status = a->status;
   p.trace = reinterpret_cast<long long*>(a->trace);
-  p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C, pl.tc, pl.ns, pl.nvh);
+  p.sm = smem_layout(pl.G, a->D, pl.CL, esize_of(a->dtype), pl.C * shards, pl.C, pl.tc, pl.ns, pl.nvh);
 
   if (pl.tc) {
     auto enc = encode_fn();

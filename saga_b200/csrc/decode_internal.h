@@ -25,10 +25,12 @@ struct ChunkStat {
 };
 
 constexpr int kCtrlInts = 32;   // control counters per group
-constexpr int kCtrlDone = 31;   // index of the group's completion counter
+constexpr int kCtrlDone = 31;   // index of the group's completion counter (this device's chunks)
+constexpr int kCtrlShardsDone = 30;  // sharded, on shard 0: devices whose chunks are all done
 constexpr int kMaxG = 32;       // query heads per key head supported
 constexpr int kMaxStages = 4;   // K-tile ring depth of the tensor-core scorer
 constexpr int kMaxGatherGroups = 64;
+constexpr int kMaxShards = 8;   // devices a sequence can be sharded over
 
 // Shared-memory carve of the fused kernel, in bytes from a 1024-aligned base.
 struct SmemLayout {
@@ -45,10 +47,11 @@ __host__ __device__ constexpr bool uses_tc_pv(bool tc, int D) { return tc && D =
 __host__ __device__ inline int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
 // G query heads per key head, head dim D, CL positions per chunk, esize bytes
-// per element, C chunks per group, tensor-core scorer with ns stages, nvh
-// value heads per group.
-__host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esize, int C, bool tc, int ns,
-                                                 int nvh) {
+// per element, C chunks per group (all devices' with sequence sharding), of
+// which c_local on this device (they split the merged outputs), tensor-core
+// scorer with ns stages, nvh value heads per group.
+__host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esize, int C, int c_local, bool tc,
+                                                 int ns, int nvh) {
   SmemLayout l;
   const int SH = G <= 16 ? 16 : 32;  // head slots per position of the logits
   const int rowb = D * esize;
@@ -56,9 +59,9 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   const int red = 8 * 8 * D * 4 + 8 * 8 * 4;  // per-warp values and weight sums
   const int hist = G * 256 * 4;
   // merge staging: (m, l) and scale per covered head and chunk, o per output and chunk
-  const int per = (G * D + C - 1) / C;
+  const int per = (G * D + c_local - 1) / c_local;
   const int nhs = per / D + 2;
-  const int merge = 4 * (nhs * C * 3 + per * C) + 256;
+  const int merge = 4 * (nhs * C * 3 + per * C + per) + 256;
   // per-chunk exchange staging, at the end of the work area: the count
   // exchange runs while value rows are landing at its start
   const int xchg = align_up(4 * C * G, 128);
@@ -117,6 +120,13 @@ struct DecodeParams {
   void* logits_out; int64_t lo_ld;
   int* ctrl; ChunkStat* stats; int* hist;
   unsigned long long* slots;  // [group][chunk][head][D + 4] epoch-tagged exchange slots
+  // sequence sharding: chunk c of a group lives on shard c / c_local; its slots
+  // are in slot_base[shard] (this device's or a peer's workspace), [group]
+  // [c % c_local][head][D + 4]; the epoch and completion counters are shard 0's
+  int nsel, pos_offset, shards, shard, c_local;
+  unsigned long long* slot_base[kMaxShards];
+  int* ctrl_home;               // shard 0's control counters (device tickets)
+  int* ctrl_peer[kMaxShards];   // every shard's control counters (epoch releases)
   int* status;
   long long* trace;
   SmemLayout sm;

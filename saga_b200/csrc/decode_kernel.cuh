@@ -76,6 +76,7 @@ struct Misc {
   int i2[kMaxG];
   int i3[kMaxG];
   float lsum[kMaxG];
+  float aux2[kMaxG];   // merge: stabiliser of the combined partial per covered head
   float thr[kMaxG];     // softmax-space thresholds of the rows (amortized)
   int gstart[kMaxGatherGroups + 1];  // gather groups: list ranges
   int gvh[kMaxGatherGroups];         // gather group -> value head
@@ -183,13 +184,15 @@ template <> struct Pair<__half> {
 // ---------------------------------------------------------------------------
 // Epoch-tagged exchange slots
 // ---------------------------------------------------------------------------
+// Slots are read by the other CTAs of the group, which with sequence sharding
+// run on other devices (peer memory): system-scope accesses.
 __device__ __forceinline__ void slot_put(unsigned long long* p, uint32_t tag, uint32_t bits) {
   const unsigned long long v = ((unsigned long long)tag << 32) | bits;
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 // All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i].
@@ -242,11 +245,36 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
   }
 }
 
-// slots_gather over `count` consecutive slots: base + i * stride. One out-of-
-// line copy serves every exchange of per-(chunk, head) scalars.
-static __device__ __noinline__ void slots_gather_linear(const unsigned long long* base, int stride, int count,
-                                                        uint32_t tag, uint32_t* dst, int* status) {
-  slots_gather(count, [&](int i) { return base + (size_t)i * stride; }, tag, dst, status);
+__device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k);
+__device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p, int g, int s, int hl, int k);
+
+// Exchange of one per-(chunk, head) scalar field of group g over this
+// device's chunks: dst[c * G + hl] for local chunk c (all of the group's
+// chunks when the sequence is not sharded). One out-of-line copy serves
+// every such exchange.
+static __device__ __noinline__ void slots_gather_field(const DecodeParams& p, int g, int field, uint32_t tag,
+                                                       uint32_t* dst) {
+  const FastDiv divg((uint32_t)p.G);
+  const int c0 = p.shards > 1 ? p.shard * p.c_local : 0;
+  slots_gather(
+      p.c_local * p.G,
+      [&](int i) {
+        const int c = (int)divg.div((uint32_t)i);
+        return slot_at(p, g, c0 + c, i - c * p.G, field);
+      },
+      tag, dst, p.status);
+}
+// The same field of every device's combined value: dst[s * G + hl].
+static __device__ __noinline__ void slots_gather_shards(const DecodeParams& p, int g, int field, uint32_t tag,
+                                                        uint32_t* dst) {
+  const FastDiv divg((uint32_t)p.G);
+  slots_gather(
+      p.shards * p.G,
+      [&](int i) {
+        const int sh = (int)divg.div((uint32_t)i);
+        return shard_slot(p, g, sh, i - sh * p.G, field);
+      },
+      tag, dst, p.status);
 }
 
 // The reference's rounding chain for one logit (attention.py:121-126).
@@ -820,9 +848,21 @@ __device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc
 
 // Slot address: group g, chunk c, local head hl, field k.
 __device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k) {
-  return p.slots + (((size_t)g * p.C + c) * p.G + hl) * (size_t)(p.D + 4) + k;
+  int owner = 0;
+  if (p.shards > 1) {  // chunk c of the group lives on shard c / c_local
+    owner = c / p.c_local;
+    c -= owner * p.c_local;
+  }
+  return p.slot_base[owner] + (((size_t)g * p.c_local + c) * p.G + hl) * (size_t)(p.D + 4) + k;
 }
 constexpr int kSlotS = 0, kSlotCnt = 1, kSlotM = 2, kSlotL = 3, kSlotO = 4;
+
+// Sequence sharding: the combined value of device s's chunks, in device s's
+// workspace past the chunk slots: [group][head][D + 4].
+__device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p, int g, int s, int hl, int k) {
+  const size_t chunk_slots = (size_t)p.B * p.Hk * p.c_local * p.G * (p.D + 4);
+  return p.slot_base[s] + chunk_slots + ((size_t)g * p.G + hl) * (size_t)(p.D + 4) + k;
+}
 
 // ---------------------------------------------------------------------------
 // V gather of one item, in two halves so that the value rows can be in flight
@@ -1445,71 +1485,108 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
 // flattened (local head, d) space. All the partials it needs are fetched in
 // one burst; sums run in chunk order.
 // ---------------------------------------------------------------------------
-template <typename T, int D, int MODE>
-__device__ void merge_slice(const DecodeParams& p, int g, int j, int b, int h0, uint8_t* scratch, Misc* misc) {
+// One merge level for outputs [lo, lo + nout) (heads hl0 .. hl0 + nhs - 1):
+// from nsrc partials (m, l per head; o per output) at src(k, hl, field),
+// misc->lsum[hh] = l and misc->aux2[hh] = m of the combination, acc[k] = o
+// relative to that m. The combination order is fixed.
+template <int D, int MODE, typename Src>
+__device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, int nout, int hl0, int nhs, uint32_t tag,
+                            uint8_t* scratch, float* acc, Misc* misc, bool final_level) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int G = p.G, C = p.C;
+  uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][nsrc][2]
+  uint32_t* ov = ml + nhs * nsrc * 2;                   // [nout][nsrc]
+  const int n_ml = nhs * nsrc * 2;
+  const FastDiv div2c((uint32_t)(2 * nsrc)), divc((uint32_t)nsrc);
+  slots_gather(
+      n_ml + nout * nsrc,
+      [&](int i) {
+        if (i < n_ml) {
+          const int hh = (int)div2c.div((uint32_t)i), r = i - hh * 2 * nsrc;
+          return src(r >> 1, hl0 + hh, kSlotM + (r & 1));
+        }
+        const int k = i - n_ml;
+        const int kq = (int)divc.div((uint32_t)k);
+        const int o = lo + kq;
+        return src(k - kq * nsrc, o / D, kSlotO + o % D);
+      },
+      tag, ml, p.status);
+  __syncthreads();
+  float* scl = reinterpret_cast<float*>(ov + nout * nsrc);  // [nhs][nsrc]
+  for (int hh = warp; hh < nhs; hh += kWarps) {
+    float M = -INFINITY;
+    for (int c = lane; c < nsrc; c += 32) M = nanmax(M, __uint_as_float(ml[(hh * nsrc + c) * 2]));
+    M = warp_nanmax(M);
+    float Ls = 0.f;
+    for (int c = lane; c < nsrc; c += 32) {
+      const float mc = __uint_as_float(ml[(hh * nsrc + c) * 2]);
+      // no source of this level has data (every m is -inf): scale 0, not
+      // exp(-inf - -inf); a row empty everywhere still ends as 0 / 0
+      const float f = (MODE == MODE_CALIBRATE) ? 1.f : (M == -INFINITY ? 0.f : __expf(mc - M));
+      scl[hh * nsrc + c] = f;
+      Ls += __uint_as_float(ml[(hh * nsrc + c) * 2 + 1]) * f;
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) {
+      // calibration renormalises by max(sum p, 1e-12) (attention.py:161)
+      misc->lsum[hh] = (MODE == MODE_CALIBRATE && final_level) ? fmaxf(Ls, 1e-12f) : Ls;
+      misc->aux2[hh] = M;
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < nout; k += kThreads) {
+    const int hh = (lo + k) / D - hl0;
+    float a = 0.f;
+    for (int c = 0; c < nsrc; ++c) a += __uint_as_float(ov[k * nsrc + c]) * scl[hh * nsrc + c];
+    acc[k] = a;
+  }
+  __syncthreads();
+}
+
+// Merge of the group's partials: the CTAs of this device split the outputs;
+// CTA jl merges outputs [jl * per, ...) over the chunks. With sequence
+// sharding this happens in two levels: first over this device's chunks, whose
+// combined partial is published; then over the devices' partials of the same
+// slice (CTA jl of every device covers the same outputs). Every device writes
+// all outputs.
+template <typename T, int D, int MODE>
+__device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0, uint8_t* scratch, Misc* misc) {
+  const int G = p.G;
   const int tot = G * D;
-  const int per = (tot + C - 1) / C;
-  const int lo = j * per, hi = min(tot, lo + per);
+  const int per = (tot + p.c_local - 1) / p.c_local;
+  const int lo = jl * per, hi = min(tot, lo + per);
   if (lo >= hi) return;
   const int hl0 = lo / D, hl1 = (hi - 1) / D;
   const int nhs = hl1 - hl0 + 1;
   const int nout = hi - lo;
   const uint32_t tag = misc->tag;
-  uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][C][2]
-  uint32_t* ov = ml + nhs * C * 2;                      // [nout][C]
-  const int n_ml = nhs * C * 2;
-  const FastDiv div2c((uint32_t)(2 * C)), divc((uint32_t)C);
-  const unsigned long long* s0 = slot_at(p, g, 0, 0, 0);
-  slots_gather(
-      n_ml + nout * C,
-      [&](int i) {
-        int c, hl, f;
-        if (i < n_ml) {
-          const int hh = (int)div2c.div((uint32_t)i), r = i - hh * 2 * C;
-          c = r >> 1;
-          hl = hl0 + hh;
-          f = kSlotM + (r & 1);
-        } else {
-          const int k = i - n_ml;
-          const int kq = (int)divc.div((uint32_t)k);
-          const int o = lo + kq;
-          c = k - kq * C;
-          hl = o / D;
-          f = kSlotO + o % D;
-        }
-        return s0 + ((size_t)c * G + hl) * (D + 4) + f;
-      },
-      tag, ml, p.status);
-  __syncthreads();
+  const bool sharded = p.shards > 1;
+  const int c0 = sharded ? p.shard * p.c_local : 0;
+  // combined outputs of the slice, past the largest staging of either level
+  // (the layout reserves nhs <= per / D + 2 heads and p.C >= either source count)
+  float* acc = reinterpret_cast<float*>(scratch) + (per / D + 2) * p.C * 3 + per * p.C;
+  merge_level<D, MODE>(
+      p, p.c_local, [&](int c, int hl, int f) { return slot_at(p, g, c0 + c, hl, f); }, lo, nout, hl0, nhs, tag,
+      scratch, acc, misc, !sharded);
   if (threadIdx.x == 0) trace_stamp(p, 15);
-  float* scl = reinterpret_cast<float*>(ov + nout * C);  // [nhs][C]
-  trace_sub(p, 20);
-  for (int hh = warp; hh < nhs; hh += kWarps) {
-    float M = -INFINITY;
-    for (int c = lane; c < C; c += 32) M = nanmax(M, __uint_as_float(ml[(hh * C + c) * 2]));
-    M = warp_nanmax(M);
-    float Ls = 0.f;
-    for (int c = lane; c < C; c += 32) {
-      const float mc = __uint_as_float(ml[(hh * C + c) * 2]);
-      const float f = (MODE == MODE_CALIBRATE) ? 1.f : __expf(mc - M);
-      scl[hh * C + c] = f;
-      Ls += __uint_as_float(ml[(hh * C + c) * 2 + 1]) * f;
+  if (sharded) {
+    for (int k = threadIdx.x; k < nout; k += kThreads) {
+      const int o = lo + k;
+      slot_put(shard_slot(p, g, p.shard, o / D, kSlotO + o % D), tag, __float_as_uint(acc[k]));
     }
-    Ls = warp_sum(Ls);
-    // calibration renormalises by max(sum p, 1e-12) (attention.py:161)
-    if (lane == 0) misc->lsum[hh] = (MODE == MODE_CALIBRATE) ? fmaxf(Ls, 1e-12f) : Ls;
+    for (int hh = threadIdx.x; hh < nhs; hh += kThreads) {
+      slot_put(shard_slot(p, g, p.shard, hl0 + hh, kSlotM), tag, __float_as_uint(misc->aux2[hh]));
+      slot_put(shard_slot(p, g, p.shard, hl0 + hh, kSlotL), tag, __float_as_uint(misc->lsum[hh]));
+    }
+    merge_level<D, MODE>(
+        p, p.shards, [&](int sh, int hl, int f) { return shard_slot(p, g, sh, hl, f); }, lo, nout, hl0, nhs, tag,
+        scratch, acc, misc, true);
   }
-  __syncthreads();
   trace_sub(p, 21);
   for (int k = threadIdx.x; k < nout; k += kThreads) {
     const int o = lo + k;
     const int hh = o / D - hl0, d = o % D;
-    float acc = 0.f;
-    for (int c = 0; c < C; ++c) acc += __uint_as_float(ov[k * C + c]) * scl[hh * C + c];
     T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + o / D) * p.o_sh + d;
-    *out = Num<T>::from_f(acc / misc->lsum[hh]);
+    *out = Num<T>::from_f(acc[k] / misc->lsum[hh]);
   }
 }
 
@@ -1609,12 +1686,13 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
   if (threadIdx.x == 0) trace_col(p, 121, (long long)globaltimer_ns());
   for (int item = blockIdx.x; item < p.items; item += gridDim.x) {
     if constexpr (TC) tc_fence_after();  // TMEM reads of the previous item precede this item's MMAs
-    const int g = item / C, j = item % C;
+    // chunk jl of this device = chunk j of the group (shard-major order)
+    const int g = item / p.c_local, jl = item % p.c_local, j = p.shard * p.c_local + jl;
     const int b = g / p.Hk, kh = g % p.Hk, h0 = kh * G;
-    const int p0 = j * CL;
-    const int n = min(p.L - p0, CL);
+    const int p0 = jl * CL;
+    const int n = min(p.nsel - p0, CL);
     const int nw = (n + 31) / 32;
-    int* ctrl = p.ctrl + (size_t)g * kCtrlInts;
+    int* ctrl = p.ctrl + (size_t)g * kCtrlInts;  // this device's counters of the group
     ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G] (calibration)
     ChunkStat* st = stg + (size_t)j * G;
     const int row0 = b * p.Hq + h0;
@@ -1720,18 +1798,30 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       for (int hl = threadIdx.x; hl < G; hl += kThreads)
         slot_put(slot_at(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
       // slot (chunk c, head hl) sits at index c * G + hl of the group's slots
-      slots_gather_linear(slot_at(p, g, 0, 0, kSlotS), D + 4, C * G, tag, xbuf, p.status);
+      slots_gather_field(p, g, kSlotS, tag, xbuf);
       __syncthreads();
       SAGA_TRACE(2)
       // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
+      if (p.shards > 1) {
+        // this device's sum, published once; the group's sum over devices
+        for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+          float s = 0.f;
+          for (int c = 0; c < p.c_local; ++c) s += __uint_as_float(xbuf[c * G + hl]);
+          if (jl == 0) slot_put(shard_slot(p, g, p.shard, hl, kSlotS), tag, __float_as_uint(s));
+        }
+        __syncthreads();
+        slots_gather_shards(p, g, kSlotS, tag, xbuf);
+        __syncthreads();
+      }
+      const int nsum = p.shards > 1 ? p.shards : p.c_local;  // partial sums in xbuf
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         float s = 0.f;
-        for (int c = 0; c < C; ++c) s += __uint_as_float(xbuf[c * G + hl]);
+        for (int c = 0; c < nsum; ++c) s += __uint_as_float(xbuf[c * G + hl]);
         s = Num<T>::round(s);
         const float thr = clamp_min_keep_nan(misc->thr[hl], 1e-30f);
         const float t = __fadd_rn(misc->m[hl], logf(__fmul_rn(thr, s)));
         misc->t[hl] = t;
-        if (j == 0) {
+        if (jl == 0) {  // this device's first chunk (every shard writes its own outputs)
           if (p.logit_thr_out) p.logit_thr_out[row0 + hl] = t;
           if (!isfinite(t)) set_status(p.status, SAGA_STATUS_NONFINITE_THR);
         }
@@ -1755,22 +1845,49 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // counts are exchanged
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
-      slots_gather_linear(slot_at(p, g, 0, 0, kSlotCnt), D + 4, C * G, tag, xbuf, p.status);
+      slots_gather_field(p, g, kSlotCnt, tag, xbuf);
       __syncthreads();
       SAGA_TRACE(4)
       // exclusive prefix in chunk order: keep the K lowest passing positions
+      if (p.shards > 1) {
+        // this device's chunks: prefix below chunk jl and total (kept in
+        // misc->i3); the total is published once; the earlier devices'
+        // totals and the group's total come from the other devices
+        for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+          int pre = 0, tot = 0;
+          for (int c = 0; c < p.c_local; ++c) {
+            const int cc = (int)xbuf[c * G + hl];
+            if (c < jl) pre += cc;
+            tot += cc;
+          }
+          misc->i3[hl] = pre;
+          if (jl == 0) slot_put(shard_slot(p, g, p.shard, hl, kSlotCnt), tag, (uint32_t)tot);
+        }
+        __syncthreads();
+        slots_gather_shards(p, g, kSlotCnt, tag, xbuf);
+        __syncthreads();
+      }
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         int pre = 0, tot = 0;
-        for (int c = 0; c < C; ++c) {
-          const int cc = (int)xbuf[c * G + hl];
-          if (c < j) pre += cc;
-          tot += cc;
+        if (p.shards > 1) {
+          pre = misc->i3[hl];
+          for (int sh = 0; sh < p.shards; ++sh) {
+            const int cc = (int)xbuf[sh * G + hl];
+            if (sh < p.shard) pre += cc;
+            tot += cc;
+          }
+        } else {
+          for (int c = 0; c < C; ++c) {
+            const int cc = (int)xbuf[c * G + hl];
+            if (c < j) pre += cc;
+            tot += cc;
+          }
         }
         const int mine = misc->i2[hl];
         pre = max(0, pre);  // bounds every offset below even if the slots were corrupt
         misc->i0[hl] = pre;
         misc->i1[hl] = max(0, min(mine, p.buf_k - pre));
-        if (j == 0) {
+        if (jl == 0) {
           if (p.count_out) p.count_out[row0 + hl] = tot;
           if (tot > p.buf_k) set_status(p.status, SAGA_STATUS_OVERFLOW);
           if (tot == 0) set_status(p.status, SAGA_STATUS_EMPTY_ROW);
@@ -1811,7 +1928,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
             const bool on = i < n && ((hmask[i] >> hl) & 1u);
             const uint32_t bal = __ballot_sync(0xffffffffu, on);
             const int k = o + __popc(bal & ((1u << lane) - 1u));
-            if (on && k < lim) dst[k] = p0 + i;
+            if (on && k < lim) dst[k] = p.pos_offset + p0 + i;
             o += __popc(bal);
           }
         }
@@ -1966,7 +2083,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     __syncthreads();
 
     // ---- merge of the group's partials, split across its chunks
-    merge_slice<T, D, MODE>(p, g, j, b, h0, work, misc);
+    merge_slice<T, D, MODE>(p, g, jl, b, h0, work, misc);
     SAGA_TRACE(6)
 
     // ---- the group's last chunk to finish advances the epoch and resets
@@ -1974,17 +2091,53 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     __syncthreads();
     SAGA_TRACE(7)
 #undef SAGA_TRACE
-    if (threadIdx.x == 0) misc->last = (atomicAdd(&ctrl[kCtrlDone], 1) == C - 1);
+    // Completion: the last of this device's chunks of the group resets the
+    // counters and advances the epoch. Sharded, that CTA also takes a ticket
+    // on shard 0; the last device's ticket advances every device's epoch,
+    // and each device's last CTA leaves only after its own epoch advanced.
+    // The device's grid stays open until then, so that no device's next
+    // launch overwrites slots that a slower device still reads.
+    if (threadIdx.x == 0) {
+      __threadfence();
+      misc->last = (atomicAdd(&ctrl[kCtrlDone], 1) == p.c_local - 1);
+    }
     __syncthreads();
     if (misc->last) {
-      if (threadIdx.x == 0) {
-        ctrl[kCtrlDone] = 0;
-        ctrl[0] = (int)tag;  // next launch's tag is tag + 1
-      }
-      for (int i = 1 + threadIdx.x; i < kCtrlDone; i += kThreads) ctrl[i] = 0;
+      for (int i = 1 + threadIdx.x; i < kCtrlShardsDone; i += kThreads) ctrl[i] = 0;
       if (MODE == MODE_CALIBRATE) {
         int* gh = p.hist + (size_t)g * 4 * G * 256;
         for (int i = threadIdx.x; i < 4 * G * 256; i += kThreads) gh[i] = 0;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        ctrl[kCtrlDone] = 0;
+        if (p.shards <= 1) {
+          __threadfence();
+          st_release_sys(&ctrl[0], (int)tag);  // next launch's tag is tag + 1
+        } else {
+          int* home = p.ctrl_home + (size_t)g * kCtrlInts;
+          __threadfence_system();
+          if (atomicAdd_system(&home[kCtrlShardsDone], 1) == p.shards - 1) {
+            home[kCtrlShardsDone] = 0;
+            __threadfence_system();
+            for (int s2 = 0; s2 < p.shards; ++s2)  // every device's epoch
+              st_release_sys(p.ctrl_peer[s2] + (size_t)g * kCtrlInts, (int)tag);
+          } else {
+            unsigned long long t0 = 0;
+            for (uint32_t it = 1; ld_acquire_sys(&ctrl[0]) != (int)tag; ++it) {
+              __nanosleep(64);
+              if ((it & 255u) == 0) {
+                const unsigned long long now = globaltimer_ns();
+                if (t0 == 0) {
+                  t0 = now;
+                } else if (now - t0 > kWaitLimitNs) {
+                  set_status(p.status, SAGA_STATUS_WAIT_TIMEOUT);
+                  break;
+                }
+              }
+            }
+          }
+        }
       }
     }
     __syncthreads();
