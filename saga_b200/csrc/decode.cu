@@ -13,9 +13,9 @@
 
 namespace saga {
 
-const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask);
-const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask);
-const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask);
+const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask, bool shard);
+const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask, bool shard);
+const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask, bool shard);
 
 namespace {
 
@@ -41,10 +41,10 @@ DevInfo dev_info() {
 
 int esize_of(int dt) { return dt == SAGA_FP32 ? 4 : 2; }
 
-const void* pick_kernel(int dt, int D, int mode, bool tc, bool mask) {
-  if (dt == SAGA_BF16) return pick_decode_kernel_bf16(D, mode, tc, mask);
-  if (dt == SAGA_FP16) return pick_decode_kernel_fp16(D, mode, tc, mask);
-  return pick_decode_kernel_fp32(D, mode, false, mask);
+const void* pick_kernel(int dt, int D, int mode, bool tc, bool mask, bool shard) {
+  if (dt == SAGA_BF16) return pick_decode_kernel_bf16(D, mode, tc, mask, shard);
+  if (dt == SAGA_FP16) return pick_decode_kernel_fp16(D, mode, tc, mask, shard);
+  return pick_decode_kernel_fp32(D, mode, false, mask, shard);
 }
 
 const char* mode_name(int mode) {
@@ -161,7 +161,11 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
     const int want = 16 * ngg * std::max(1, std::min(4, 256 / (16 * ngg)));
     while (pl->tmem_cols < want) pl->tmem_cols *= 2;  // ngg <= 16 on this path: at most 256
   }
-  const void* kfn = pick_kernel(a->dtype, a->D, mode, tc, a->mask != nullptr);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, tc, a->mask != nullptr, shards > 1);
+  if (!kfn) {
+    *err = "no kernel for this combination of dtype, head_dim, op and sharding";
+    return SAGA_ERR_UNSUPPORTED;
+  }
   // The CTAs on one SM must fit its 512 TMEM columns together (an allocation
   // that does not fit would wait): ask for enough shared memory that no more
   // of them share an SM.
@@ -287,7 +291,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     }
   }
 
-  const void* kfn = pick_kernel(a->dtype, a->D, mode, pl.tc, a->mask != nullptr);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, pl.tc, a->mask != nullptr, shards > 1);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(kThreads);

@@ -4,9 +4,13 @@
 
 namespace saga {
 
-const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask) {
-  if (tc) return mask ? pick_d_mode<__nv_bfloat16, true, true>(D, mode) : pick_d_mode<__nv_bfloat16, true, false>(D, mode);
-  return mask ? pick_d_mode<__nv_bfloat16, false, true>(D, mode) : pick_d_mode<__nv_bfloat16, false, false>(D, mode);
+const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask, bool shard) {
+  if (shard) {
+    if (!tc) return nullptr;
+    return mask ? pick_d_mode<__nv_bfloat16, true, true, true>(D, mode) : pick_d_mode<__nv_bfloat16, true, false, true>(D, mode);
+  }
+  if (tc) return mask ? pick_d_mode<__nv_bfloat16, true, true, false>(D, mode) : pick_d_mode<__nv_bfloat16, true, false, false>(D, mode);
+  return mask ? pick_d_mode<__nv_bfloat16, false, true, false>(D, mode) : pick_d_mode<__nv_bfloat16, false, false, false>(D, mode);
 }
 
 }  // namespace saga

@@ -4,9 +4,13 @@
 
 namespace saga {
 
-const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask) {
-  if (tc) return mask ? pick_d_mode<__half, true, true>(D, mode) : pick_d_mode<__half, true, false>(D, mode);
-  return mask ? pick_d_mode<__half, false, true>(D, mode) : pick_d_mode<__half, false, false>(D, mode);
+const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask, bool shard) {
+  if (shard) {
+    if (!tc) return nullptr;
+    return mask ? pick_d_mode<__half, true, true, true>(D, mode) : pick_d_mode<__half, true, false, true>(D, mode);
+  }
+  if (tc) return mask ? pick_d_mode<__half, true, true, false>(D, mode) : pick_d_mode<__half, true, false, false>(D, mode);
+  return mask ? pick_d_mode<__half, false, true, false>(D, mode) : pick_d_mode<__half, false, false, false>(D, mode);
 }
 
 }  // namespace saga

@@ -4,8 +4,9 @@
 
 namespace saga {
 
-const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask) {
-  return mask ? pick_d_mode<float, false, true>(D, mode) : pick_d_mode<float, false, false>(D, mode);
+const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask, bool shard) {
+  if (shard) return nullptr;  // sequence sharding runs on the tensor-core path only
+  return mask ? pick_d_mode<float, false, true, false>(D, mode) : pick_d_mode<float, false, false, false>(D, mode);
 }
 
 }  // namespace saga

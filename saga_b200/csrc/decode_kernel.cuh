@@ -184,15 +184,23 @@ template <> struct Pair<__half> {
 // ---------------------------------------------------------------------------
 // Epoch-tagged exchange slots
 // ---------------------------------------------------------------------------
-// Slots are read by the other CTAs of the group, which with sequence sharding
-// run on other devices (peer memory): system-scope accesses.
+// Slots are read by the other CTAs of the group: GPU scope, or system scope
+// when the sequence is sharded and the readers run on other devices (SHD).
+template <bool SHD>
 __device__ __forceinline__ void slot_put(unsigned long long* p, uint32_t tag, uint32_t bits) {
   const unsigned long long v = ((unsigned long long)tag << 32) | bits;
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+  if constexpr (SHD)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+  else
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
+template <bool SHD>
 __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  if constexpr (SHD)
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 // All threads: fetch `count` slots (addresses from `addr(i)`) into dst[i].
@@ -200,7 +208,7 @@ __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* 
 // re-polls all of its pending slots together, so a late publisher costs one
 // round trip, not one per slot. Bounded: after kWaitLimitNs the status word
 // gets SAGA_STATUS_WAIT_TIMEOUT and the stale values are used.
-template <typename AddrFn>
+template <bool SHD, typename AddrFn>
 __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t tag, uint32_t* dst, int* status) {
   for (int base = threadIdx.x; base < count; base += kThreads * 8) {
     const unsigned long long* a[8];
@@ -213,7 +221,7 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
       if (i < count) pending |= 1u << k;
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = ((pending >> k) & 1u) ? slot_ld(a[k]) : 0ull;
+    for (int k = 0; k < 8; ++k) v[k] = ((pending >> k) & 1u) ? slot_ld<SHD>(a[k]) : 0ull;
     unsigned long long t0 = 0;
 #pragma unroll 1
     for (uint32_t it = 1;; ++it) {
@@ -240,11 +248,12 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
       __nanosleep(32);
 #pragma unroll
       for (int k = 0; k < 8; ++k)
-        if ((pending >> k) & 1u) v[k] = slot_ld(a[k]);
+        if ((pending >> k) & 1u) v[k] = slot_ld<SHD>(a[k]);
     }
   }
 }
 
+template <bool SHD>
 __device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k);
 __device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p, int g, int s, int hl, int k);
 
@@ -252,15 +261,16 @@ __device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p,
 // device's chunks: dst[c * G + hl] for local chunk c (all of the group's
 // chunks when the sequence is not sharded). One out-of-line copy serves
 // every such exchange.
+template <bool SHD>
 static __device__ __noinline__ void slots_gather_field(const DecodeParams& p, int g, int field, uint32_t tag,
                                                        uint32_t* dst) {
   const FastDiv divg((uint32_t)p.G);
-  const int c0 = p.shards > 1 ? p.shard * p.c_local : 0;
-  slots_gather(
+  const int c0 = SHD ? p.shard * p.c_local : 0;
+  slots_gather<SHD>(
       p.c_local * p.G,
       [&](int i) {
         const int c = (int)divg.div((uint32_t)i);
-        return slot_at(p, g, c0 + c, i - c * p.G, field);
+        return slot_at<SHD>(p, g, c0 + c, i - c * p.G, field);
       },
       tag, dst, p.status);
 }
@@ -268,7 +278,7 @@ static __device__ __noinline__ void slots_gather_field(const DecodeParams& p, in
 static __device__ __noinline__ void slots_gather_shards(const DecodeParams& p, int g, int field, uint32_t tag,
                                                         uint32_t* dst) {
   const FastDiv divg((uint32_t)p.G);
-  slots_gather(
+  slots_gather<true>(
       p.shards * p.G,
       [&](int i) {
         const int sh = (int)divg.div((uint32_t)i);
@@ -847,9 +857,10 @@ __device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc
 }
 
 // Slot address: group g, chunk c, local head hl, field k.
+template <bool SHD>
 __device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k) {
   int owner = 0;
-  if (p.shards > 1) {  // chunk c of the group lives on shard c / c_local
+  if constexpr (SHD) {  // chunk c of the group lives on shard c / c_local
     owner = c / p.c_local;
     c -= owner * p.c_local;
   }
@@ -1260,7 +1271,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
 // accumulates out^T[d][head slot] += V^T[d][slot] * W[slot][head slot] into 16
 // TMEM columns per gather group. The partial (m, l, o[D]) of every head is
 // then published through the group's tagged slots.
-template <typename T, int D, int MODE>
+template <typename T, int D, int MODE, bool SHD>
 __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0, const T* __restrict__ sc,
                               const uint32_t* __restrict__ hmask, const uint32_t* __restrict__ list,
                               uint8_t* __restrict__ work, uint8_t* __restrict__ wpv, Misc* misc, uint32_t tmem_base,
@@ -1364,21 +1375,21 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
       }
 #pragma unroll
       for (int hh = 0; hh < 8; ++hh)
-        if (hh < nh) slot_put(slot_at(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(o[hh]));
+        if (hh < nh) slot_put<SHD>(slot_at<SHD>(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(o[hh]));
     }
     tc_fence_before();
   }
   for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) {
     const int gi = t >> 3, hh = t & 7;
     if (hh < (misc->ghb[gi] >> 16))
-      slot_put(slot_at(p, g, j, (misc->ghb[gi] & 0xFFFF) + hh, kSlotL), tag, __float_as_uint(misc->lacc[t]));
+      slot_put<SHD>(slot_at<SHD>(p, g, j, (misc->ghb[gi] & 0xFFFF) + hh, kSlotL), tag, __float_as_uint(misc->lacc[t]));
   }
   for (int hl = threadIdx.x; hl < G; hl += kThreads)
-    slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
+    slot_put<SHD>(slot_at<SHD>(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
   if (tr) trace_stamp(p, 14);
 }
 
-template <typename T, int D, int MODE>
+template <typename T, int D, int MODE, bool SHD>
 __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, int p0, int n,
                            const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
                            const uint32_t* __restrict__ list, uint8_t* __restrict__ work, float* __restrict__ wbuf,
@@ -1470,13 +1481,13 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
         float s = 0.f;
 #pragma unroll
         for (int wp = 0; wp < kWarps; ++wp) s += red[wp * (D + 1) + d];
-        slot_put(slot_at(p, g, j, hb + hh, d < D ? kSlotO + d : kSlotL), tag, __float_as_uint(s));
+        slot_put<SHD>(slot_at<SHD>(p, g, j, hb + hh, d < D ? kSlotO + d : kSlotL), tag, __float_as_uint(s));
       }
       __syncthreads();
     }
   }
   for (int hl = threadIdx.x; hl < G; hl += kThreads)
-    slot_put(slot_at(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
+    slot_put<SHD>(slot_at<SHD>(p, g, j, hl, kSlotM), tag, __float_as_uint(MODE == MODE_CALIBRATE ? 0.f : misc->aux[hl]));
   if (tr) trace_stamp(p, 14);
 }
 
@@ -1487,17 +1498,18 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
 // ---------------------------------------------------------------------------
 // One merge level for outputs [lo, lo + nout) (heads hl0 .. hl0 + nhs - 1):
 // from nsrc partials (m, l per head; o per output) at src(k, hl, field),
-// misc->lsum[hh] = l and misc->aux2[hh] = m of the combination, acc[k] = o
-// relative to that m. The combination order is fixed.
-template <int D, int MODE, typename Src>
+// misc->lsum[hh] = l and misc->aux2[hh] = m of the combination, and
+// emit(k, o, hh) for every output with o relative to that m. The
+// combination order is fixed.
+template <int D, int MODE, bool SHD, typename Src, typename Emit>
 __device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, int nout, int hl0, int nhs, uint32_t tag,
-                            uint8_t* scratch, float* acc, Misc* misc, bool final_level) {
+                            uint8_t* scratch, Emit emit, Misc* misc, bool final_level) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][nsrc][2]
   uint32_t* ov = ml + nhs * nsrc * 2;                   // [nout][nsrc]
   const int n_ml = nhs * nsrc * 2;
   const FastDiv div2c((uint32_t)(2 * nsrc)), divc((uint32_t)nsrc);
-  slots_gather(
+  slots_gather<SHD>(
       n_ml + nout * nsrc,
       [&](int i) {
         if (i < n_ml) {
@@ -1537,9 +1549,8 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, in
     const int hh = (lo + k) / D - hl0;
     float a = 0.f;
     for (int c = 0; c < nsrc; ++c) a += __uint_as_float(ov[k * nsrc + c]) * scl[hh * nsrc + c];
-    acc[k] = a;
+    emit(k, a, hh);
   }
-  __syncthreads();
 }
 
 // Merge of the group's partials: the CTAs of this device split the outputs;
@@ -1548,7 +1559,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, in
 // combined partial is published; then over the devices' partials of the same
 // slice (CTA jl of every device covers the same outputs). Every device writes
 // all outputs.
-template <typename T, int D, int MODE>
+template <typename T, int D, int MODE, bool SHD>
 __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0, uint8_t* scratch, Misc* misc) {
   const int G = p.G;
   const int tot = G * D;
@@ -1559,35 +1570,39 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
   const int nhs = hl1 - hl0 + 1;
   const int nout = hi - lo;
   const uint32_t tag = misc->tag;
-  const bool sharded = p.shards > 1;
-  const int c0 = sharded ? p.shard * p.c_local : 0;
-  // combined outputs of the slice, past the largest staging of either level
-  // (the layout reserves nhs <= per / D + 2 heads and p.C >= either source count)
-  float* acc = reinterpret_cast<float*>(scratch) + (per / D + 2) * p.C * 3 + per * p.C;
-  merge_level<D, MODE>(
-      p, p.c_local, [&](int c, int hl, int f) { return slot_at(p, g, c0 + c, hl, f); }, lo, nout, hl0, nhs, tag,
-      scratch, acc, misc, !sharded);
-  if (threadIdx.x == 0) trace_stamp(p, 15);
-  if (sharded) {
-    for (int k = threadIdx.x; k < nout; k += kThreads) {
+  const int c0 = SHD ? p.shard * p.c_local : 0;
+  // the group's output of this slice, normalised by the combined weight sum
+  const auto write_out = [&](int k, float a, int hh) {
+    const int o = lo + k;
+    T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + o / D) * p.o_sh + o % D;
+    *out = Num<T>::from_f(a / misc->lsum[hh]);
+  };
+  if constexpr (!SHD) {
+    merge_level<D, MODE, false>(
+        p, p.c_local, [&](int c, int hl, int f) { return slot_at<false>(p, g, c, hl, f); }, lo, nout, hl0, nhs, tag,
+        scratch, write_out, misc, true);
+    if (threadIdx.x == 0) trace_stamp(p, 15);
+  } else {
+    // this device's chunks; their combined partial of the slice is published
+    const auto publish = [&](int k, float a, int) {
       const int o = lo + k;
-      slot_put(shard_slot(p, g, p.shard, o / D, kSlotO + o % D), tag, __float_as_uint(acc[k]));
-    }
+      slot_put<true>(shard_slot(p, g, p.shard, o / D, kSlotO + o % D), tag, __float_as_uint(a));
+    };
+    merge_level<D, MODE, true>(
+        p, p.c_local, [&](int c, int hl, int f) { return slot_at<true>(p, g, c0 + c, hl, f); }, lo, nout, hl0, nhs,
+        tag, scratch, publish, misc, false);
     for (int hh = threadIdx.x; hh < nhs; hh += kThreads) {
-      slot_put(shard_slot(p, g, p.shard, hl0 + hh, kSlotM), tag, __float_as_uint(misc->aux2[hh]));
-      slot_put(shard_slot(p, g, p.shard, hl0 + hh, kSlotL), tag, __float_as_uint(misc->lsum[hh]));
+      slot_put<true>(shard_slot(p, g, p.shard, hl0 + hh, kSlotM), tag, __float_as_uint(misc->aux2[hh]));
+      slot_put<true>(shard_slot(p, g, p.shard, hl0 + hh, kSlotL), tag, __float_as_uint(misc->lsum[hh]));
     }
-    merge_level<D, MODE>(
+    __syncthreads();  // the staging is reused below
+    if (threadIdx.x == 0) trace_stamp(p, 15);
+    // every device's partial of the same slice
+    merge_level<D, MODE, true>(
         p, p.shards, [&](int sh, int hl, int f) { return shard_slot(p, g, sh, hl, f); }, lo, nout, hl0, nhs, tag,
-        scratch, acc, misc, true);
+        scratch, write_out, misc, true);
   }
   trace_sub(p, 21);
-  for (int k = threadIdx.x; k < nout; k += kThreads) {
-    const int o = lo + k;
-    const int hh = o / D - hl0, d = o % D;
-    T* out = reinterpret_cast<T*>(p.out) + (int64_t)b * p.o_sb + (int64_t)(h0 + o / D) * p.o_sh + d;
-    *out = Num<T>::from_f(acc[k] / misc->lsum[hh]);
-  }
 }
 
 // Radix select: warp-parallel search of the bin holding the `want`-th largest
@@ -1632,7 +1647,7 @@ __device__ __forceinline__ int find_bin(const int* hist256, int want, int* above
 // ---------------------------------------------------------------------------
 // The fused kernel.
 // ---------------------------------------------------------------------------
-template <typename T, int D, int MODE, bool TC, bool MASK>
+template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD>
 __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-aligned base (the 128-B swizzle pattern is taken from address bits)
@@ -1796,24 +1811,24 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     if constexpr (MODE == MODE_AMORTIZED) {
       // exchange the partial exp-sums (attention.py:145: sum over the row)
       for (int hl = threadIdx.x; hl < G; hl += kThreads)
-        slot_put(slot_at(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
+        slot_put<SHD>(slot_at<SHD>(p, g, j, hl, kSlotS), tag, __float_as_uint(misc->s[hl]));
       // slot (chunk c, head hl) sits at index c * G + hl of the group's slots
-      slots_gather_field(p, g, kSlotS, tag, xbuf);
+      slots_gather_field<SHD>(p, g, kSlotS, tag, xbuf);
       __syncthreads();
       SAGA_TRACE(2)
       // logit threshold t = m + log(max(thr, 1e-30) * s)  (attention.py:147)
-      if (p.shards > 1) {
+      if constexpr (SHD) {
         // this device's sum, published once; the group's sum over devices
         for (int hl = threadIdx.x; hl < G; hl += kThreads) {
           float s = 0.f;
           for (int c = 0; c < p.c_local; ++c) s += __uint_as_float(xbuf[c * G + hl]);
-          if (jl == 0) slot_put(shard_slot(p, g, p.shard, hl, kSlotS), tag, __float_as_uint(s));
+          if (jl == 0) slot_put<SHD>(shard_slot(p, g, p.shard, hl, kSlotS), tag, __float_as_uint(s));
         }
         __syncthreads();
         slots_gather_shards(p, g, kSlotS, tag, xbuf);
         __syncthreads();
       }
-      const int nsum = p.shards > 1 ? p.shards : p.c_local;  // partial sums in xbuf
+      const int nsum = SHD ? p.shards : p.c_local;  // partial sums in xbuf
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         float s = 0.f;
         for (int c = 0; c < nsum; ++c) s += __uint_as_float(xbuf[c * G + hl]);
@@ -1839,17 +1854,17 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 #pragma unroll
         for (int wp = 0; wp < kWarps; ++wp) cnt += misc->cntw[wp][hl];
         misc->i2[hl] = cnt;
-        slot_put(slot_at(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
+        slot_put<SHD>(slot_at<SHD>(p, g, j, hl, kSlotCnt), tag, (uint32_t)cnt);
       }
       // lists, value-row copies and the first pass's weights go out while the
       // counts are exchanged
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
-      slots_gather_field(p, g, kSlotCnt, tag, xbuf);
+      slots_gather_field<SHD>(p, g, kSlotCnt, tag, xbuf);
       __syncthreads();
       SAGA_TRACE(4)
       // exclusive prefix in chunk order: keep the K lowest passing positions
-      if (p.shards > 1) {
+      if constexpr (SHD) {
         // this device's chunks: prefix below chunk jl and total (kept in
         // misc->i3); the total is published once; the earlier devices'
         // totals and the group's total come from the other devices
@@ -1861,7 +1876,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
             tot += cc;
           }
           misc->i3[hl] = pre;
-          if (jl == 0) slot_put(shard_slot(p, g, p.shard, hl, kSlotCnt), tag, (uint32_t)tot);
+          if (jl == 0) slot_put<SHD>(shard_slot(p, g, p.shard, hl, kSlotCnt), tag, (uint32_t)tot);
         }
         __syncthreads();
         slots_gather_shards(p, g, kSlotCnt, tag, xbuf);
@@ -1869,7 +1884,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         int pre = 0, tot = 0;
-        if (p.shards > 1) {
+        if constexpr (SHD) {
           pre = misc->i3[hl];
           for (int sh = 0; sh < p.shards; ++sh) {
             const int cc = (int)xbuf[sh * G + hl];
@@ -1938,10 +1953,10 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         // heads capped at K changed their bits and stabiliser: redo their weights
         pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, misc->ngroups, 0,
                             min(misc->gpad[misc->ngroups], p.sm.brw), true);
-        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, true);
+        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, true);
       }
       else
-        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else if constexpr (MODE == MODE_CALIBRATE) {
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
@@ -2070,20 +2085,20 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       __syncthreads();
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
-        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else
-        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
       gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
-        gather_end_tc<T, D, MODE>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else
-        gather_end<T, D, MODE>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     }
     __syncthreads();
 
     // ---- merge of the group's partials, split across its chunks
-    merge_slice<T, D, MODE>(p, g, jl, b, h0, work, misc);
+    merge_slice<T, D, MODE, SHD>(p, g, jl, b, h0, work, misc);
     SAGA_TRACE(6)
 
     // ---- the group's last chunk to finish advances the epoch and resets
@@ -2111,9 +2126,9 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       __syncthreads();
       if (threadIdx.x == 0) {
         ctrl[kCtrlDone] = 0;
-        if (p.shards <= 1) {
+        if constexpr (!SHD) {
           __threadfence();
-          st_release_sys(&ctrl[0], (int)tag);  // next launch's tag is tag + 1
+          ctrl[0] = (int)tag;  // next launch's tag is tag + 1 (stream-ordered: GPU scope is enough)
         } else {
           int* home = p.ctrl_home + (size_t)g * kCtrlInts;
           __threadfence_system();
@@ -2154,27 +2169,40 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 }
 
 
-// Kernel entry of one (dtype, head_dim, mode, scorer, mask) combination.
-template <typename T, int D, int MODE, bool TC, bool MASK>
+// Kernel entry of one (dtype, head_dim, mode, scorer, mask, sharded) combination.
+template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD>
 const void* decode_kernel_ptr() {
-  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE, TC, MASK>);
+  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE, TC, MASK, SHD>);
 }
 
-template <typename T, bool TC, bool MASK>
+// Sharded kernels exist for the decode and dense modes on the tensor-core path.
+template <typename T, bool TC, bool MASK, bool SHD>
 const void* pick_d_mode(int D, int mode) {
-  if (D == 64) {
-    switch (mode) {
-      case MODE_AMORTIZED: return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK>();
-      case MODE_CALIBRATE: return decode_kernel_ptr<T, 64, MODE_CALIBRATE, TC, MASK>();
-      case MODE_DENSE: return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK>();
-      default: return decode_kernel_ptr<T, 64, MODE_LOGITS, TC, MASK>();
+  if constexpr (SHD) {
+    if (!TC) return nullptr;
+    if (D == 64) {
+      if (mode == MODE_AMORTIZED) return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK, true>();
+      if (mode == MODE_DENSE) return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK, true>();
+      return nullptr;
     }
-  }
-  switch (mode) {
-    case MODE_AMORTIZED: return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK>();
-    case MODE_CALIBRATE: return decode_kernel_ptr<T, 128, MODE_CALIBRATE, TC, MASK>();
-    case MODE_DENSE: return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK>();
-    default: return decode_kernel_ptr<T, 128, MODE_LOGITS, TC, MASK>();
+    if (mode == MODE_AMORTIZED) return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK, true>();
+    if (mode == MODE_DENSE) return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK, true>();
+    return nullptr;
+  } else {
+    if (D == 64) {
+      switch (mode) {
+        case MODE_AMORTIZED: return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK, false>();
+        case MODE_CALIBRATE: return decode_kernel_ptr<T, 64, MODE_CALIBRATE, TC, MASK, false>();
+        case MODE_DENSE: return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK, false>();
+        default: return decode_kernel_ptr<T, 64, MODE_LOGITS, TC, MASK, false>();
+      }
+    }
+    switch (mode) {
+      case MODE_AMORTIZED: return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK, false>();
+      case MODE_CALIBRATE: return decode_kernel_ptr<T, 128, MODE_CALIBRATE, TC, MASK, false>();
+      case MODE_DENSE: return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK, false>();
+      default: return decode_kernel_ptr<T, 128, MODE_LOGITS, TC, MASK, false>();
+    }
   }
 }
 
