@@ -55,6 +55,7 @@ typedef enum {
 #define SAGA_STATUS_NONFINITE_THR 0x2  /* some row's logit threshold was NaN/inf */
 #define SAGA_STATUS_OVERFLOW 0x4       /* some row had more than K passing positions */
 #define SAGA_STATUS_EMPTY_ROW 0x8      /* some row selected nothing (output is NaN) */
+#define SAGA_STATUS_APPEND_RANGE 0x10  /* append_pos_dev held a position outside [0, L): no append */
 
 /* Descriptor shared by the attention entry points. Unused fields are ignored.
  * Strides are in elements. */
@@ -122,6 +123,12 @@ typedef struct SagaAttnArgs {
   int32_t shards;
   int32_t shard;
   void* shard_workspaces[8];
+
+  /* Optional: device address of the append position (int64, first element),
+   * read by the kernel instead of append_pos, so that a CUDA graph can replay
+   * the append at a position that advances (an HF static cache's length).
+   * Not with shards > 1. */
+  const int64_t* append_pos_dev;
 } SagaAttnArgs;
 
 /* Ops understood by saga_workspace_bytes. */

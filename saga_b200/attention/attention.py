@@ -76,10 +76,23 @@ def _mask(attention_mask, key):
 # Dense decode -- attention.py:64-85
 # =============================================================================
 
+def _pending(key):
+    """Decode token recorded by SagaStaticCache for this key cache (or None)."""
+    try:
+        from .cache import take_pending
+    except Exception:  # pragma: no cover - transformers missing
+        return None
+    return take_pending(key)
+
+
 def full_einsum_forward(query, key, value, attention_mask=None, is_causal=False, scaling=None):
     """Dense GQA decode with asymmetric key/value head counts -> [B, Hq, 1, D]."""
     if query.shape[2] != 1:
         raise NotImplementedError("saga_b200 full_einsum_forward serves decode (one query position)")
+    pend = _pending(key)
+    if pend is not None:
+        return torch.ops.saga.dense_decode_append(query, key, value, _mask(attention_mask, key),
+                                                  _ops.scaling_or_default(query, scaling), *pend)
     return torch.ops.saga.dense_decode(query, key, value, _mask(attention_mask, key),
                                        _ops.scaling_or_default(query, scaling))
 
@@ -150,6 +163,11 @@ def approx_top_n_attention_amortized_cal(query, key, value, attention_mask=None,
     AMORTIZED_THRESHOLD_TENSOR[layer_idx]."""
     b, q_h, l_q, d = query.shape
     thr = _threshold_row(layer_idx, b * q_h)
+    pend = _pending(key)
+    if pend is not None:
+        return torch.ops.saga.atopn_calibrate_append(query, key, value, _mask(attention_mask, key), thr,
+                                                     int(top_n_attention), _ops.scaling_or_default(query, scaling),
+                                                     *pend)
     return torch.ops.saga.atopn_calibrate(query, key, value, _mask(attention_mask, key), thr,
                                           int(top_n_attention), _ops.scaling_or_default(query, scaling))
 
@@ -159,5 +177,10 @@ def approx_top_n_attention_amortized(query, key, value, attention_mask=None, is_
     """Later decode steps (attention.py:192-209): cached thresholds, one fused kernel."""
     b, q_h, l_q, d = query.shape
     thr = _threshold_row(layer_idx, b * q_h)
+    pend = _pending(key)
+    if pend is not None:
+        return torch.ops.saga.atopn_decode_append(query, key, value, _mask(attention_mask, key), thr,
+                                                  int(top_n_attention), _ops.scaling_or_default(query, scaling),
+                                                  *pend)
     return torch.ops.saga.atopn_decode(query, key, value, _mask(attention_mask, key), thr,
                                        int(top_n_attention), _ops.scaling_or_default(query, scaling))

@@ -82,7 +82,10 @@ int check_attn(const SagaAttnArgs* a, int op) {
   }
   if (a->k_new || a->v_new) {
     if (!a->k_new || !a->v_new) return fail(SAGA_ERR_INVALID, "k_new and v_new go together");
-    if (a->append_pos < 0 || a->append_pos >= a->L) return fail(SAGA_ERR_INVALID, "append_pos outside [0, L)");
+    if (!a->append_pos_dev && (a->append_pos < 0 || a->append_pos >= a->L))
+      return fail(SAGA_ERR_INVALID, "append_pos outside [0, L)");
+    if (a->append_pos_dev && a->shards > 1)
+      return fail(SAGA_ERR_UNSUPPORTED, "a device-side append position is not supported with sharding");
   }
   return SAGA_OK;
 }

@@ -241,6 +241,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   p.k_new = a->k_new; p.kn_sb = a->kn_sb; p.kn_sh = a->kn_sh;
   p.v_new = a->v_new; p.vn_sb = a->vn_sb; p.vn_sh = a->vn_sh;
   p.append_pos = a->append_pos;
+  p.append_pos_dev = reinterpret_cast<const long long*>(a->append_pos_dev);
   p.logit_thr_out = a->logit_thr_out; p.count_out = a->count_out;
   p.sel_idx_out = a->sel_idx_out; p.sel_ld = a->sel_ld;
   p.logits_out = a->logits_out; p.lo_ld = a->lo_ld;

@@ -116,6 +116,7 @@ struct DecodeParams {
   const void* k_new; int64_t kn_sb, kn_sh;
   const void* v_new; int64_t vn_sb, vn_sh;
   int append_pos;
+  const long long* append_pos_dev;  // when set, the append position is read from here
   float* logit_thr_out; int* count_out; int* sel_idx_out; int sel_ld;
   void* logits_out; int64_t lo_ld;
   int* ctrl; ChunkStat* stats; int* hist;

@@ -1723,8 +1723,14 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     // Every chunk of the group writes the new key row (the same values) before
     // it reads the cache, because every chunk scores the tail positions; the
     // chunk that owns the position also writes the value rows it gathers.
-    if (p.k_new) {
-      const int pos = p.append_pos;
+    int apos = p.append_pos;
+    if (p.append_pos_dev) {
+      const long long pd = p.append_pos_dev[0];
+      apos = (pd >= 0 && pd < p.L) ? (int)pd : -1;
+      if (apos < 0 && threadIdx.x == 0 && jl == 0) set_status(p.status, SAGA_STATUS_APPEND_RANGE);
+    }
+    if (p.k_new && apos >= 0) {
+      const int pos = apos;
       const T* src = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.kn_sb + (int64_t)kh * p.kn_sh;
       T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh +
                (int64_t)pos * p.k_sl;

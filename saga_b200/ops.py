@@ -137,7 +137,14 @@ def _set_append(a, k_new, v_new, append_pos):
         raise ValueError("k_new / v_new need a unit stride along head_dim")
     a.k_new, a.kn_sb, a.kn_sh = k_new.data_ptr(), k_new.stride(0), k_new.stride(1)
     a.v_new, a.vn_sb, a.vn_sh = v_new.data_ptr(), v_new.stride(0), v_new.stride(1)
-    a.append_pos = int(append_pos)
+    if isinstance(append_pos, torch.Tensor):
+        # read on the device by the kernel (a CUDA graph can replay an advancing position)
+        if not append_pos.is_cuda or append_pos.dtype != torch.int64 or append_pos.numel() < 1:
+            raise ValueError("a tensor append position must be a CUDA int64 tensor")
+        a.append_pos = 0
+        a.append_pos_dev = append_pos.data_ptr()
+    else:
+        a.append_pos = int(append_pos)
 
 
 def _out_like(q):
@@ -392,6 +399,48 @@ def _op_kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Ten
 @_op_kv_append.register_fake
 def _(k_cache, v_cache, k_new, v_new, pos):
     return None
+
+
+# The same steps with the decode token's key/value rows appended in the fused
+# kernel (the caches are written in place at the device-side position `pos`).
+@torch.library.custom_op("saga::atopn_decode_append", mutates_args=("key", "value"))
+def _op_atopn_decode_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                            attention_mask: Optional[torch.Tensor], threshold: torch.Tensor, top_n: int,
+                            scaling: float, k_new: torch.Tensor, v_new: torch.Tensor,
+                            pos: torch.Tensor) -> torch.Tensor:
+    return atopn_decode(query, key, value, attention_mask, threshold, top_n, scaling, k_new=k_new, v_new=v_new,
+                        append_pos=pos)
+
+
+@_op_atopn_decode_append.register_fake
+def _(query, key, value, attention_mask, threshold, top_n, scaling, k_new, v_new, pos):
+    return query.new_empty((query.shape[0], query.shape[1], 1, query.shape[3]))
+
+
+@torch.library.custom_op("saga::atopn_calibrate_append", mutates_args=("key", "value", "threshold_out"))
+def _op_atopn_calibrate_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                               attention_mask: Optional[torch.Tensor], threshold_out: torch.Tensor, top_n: int,
+                               scaling: float, k_new: torch.Tensor, v_new: torch.Tensor,
+                               pos: torch.Tensor) -> torch.Tensor:
+    return atopn_calibrate(query, key, value, attention_mask, threshold_out, top_n, scaling, k_new=k_new,
+                           v_new=v_new, append_pos=pos)
+
+
+@_op_atopn_calibrate_append.register_fake
+def _(query, key, value, attention_mask, threshold_out, top_n, scaling, k_new, v_new, pos):
+    return query.new_empty((query.shape[0], query.shape[1], 1, query.shape[3]))
+
+
+@torch.library.custom_op("saga::dense_decode_append", mutates_args=("key", "value"))
+def _op_dense_decode_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                            attention_mask: Optional[torch.Tensor], scaling: float, k_new: torch.Tensor,
+                            v_new: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+    return dense_decode(query, key, value, attention_mask, scaling, k_new=k_new, v_new=v_new, append_pos=pos)
+
+
+@_op_dense_decode_append.register_fake
+def _(query, key, value, attention_mask, scaling, k_new, v_new, pos):
+    return query.new_empty((query.shape[0], query.shape[1], 1, query.shape[3]))
 
 
 def scaling_or_default(query: torch.Tensor, scaling) -> float:
