@@ -12,6 +12,12 @@ The position stays on the device (copied from the cache's running length),
 so that CUDA-graph replays of the decode step append at the advancing
 position. Use this cache only with the saga_b200 attention functions: a
 recorded token that no attention call consumes raises on the next update.
+
+Key and value heads may differ (a model whose key projection was merged to
+fewer heads, speedup.py:88-116): each cache is sized from the states it first
+receives. transformers' StaticLayer sizes the values with the key-head count,
+which is why the reference rebuilds the cache tensors by hand
+(speedup.py:119-139); this cache needs no such step.
 """
 from __future__ import annotations
 
@@ -30,6 +36,15 @@ def take_pending(key: torch.Tensor) -> Optional[Tuple[torch.Tensor, torch.Tensor
 
 
 class SagaStaticLayer(StaticLayer):
+    def lazy_initialization(self, key_states: torch.Tensor, value_states: torch.Tensor) -> None:
+        super().lazy_initialization(key_states, value_states)
+        hv = value_states.shape[1]
+        if self.values.shape[1] != hv:
+            self.values = torch.zeros((self.max_batch_size, hv, self.max_cache_len, self.v_head_dim),
+                                      dtype=self.dtype, device=self.device)
+            if not torch.compiler.is_compiling():
+                torch._dynamo.mark_static_address(self.values)
+
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, *args, **kwargs):
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)

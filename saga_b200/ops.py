@@ -67,7 +67,7 @@ def read_status(device="cuda", reset: bool = True) -> int:
         if v & L.STATUS_WAIT_TIMEOUT:
             # a wait gave up: counters may be left non-zero, rebuild workspaces
             for k in [k for k in _WORKSPACES if k[0] == t.device.index]:
-                _WORKSPACES[k].zero_()
+                _WORKSPACES[k][0].zero_()
     return v
 
 
@@ -79,13 +79,22 @@ def _workspace(args: L.SagaAttnArgs, op: int, device: torch.device) -> torch.Ten
     nbytes = L.lib.saga_workspace_bytes(ctypes.byref(args), op)
     if nbytes == 0:
         raise L.SagaError(L.SAGA_ERR_INVALID, "saga_workspace_bytes")
-    # A workspace's layout depends on the shapes, so one is kept per shape.
-    key = (device.index, op, args.dtype, args.B, args.Hq, args.Hk, args.Hv, args.D, args.L)
-    ws = _WORKSPACES.get(key)
-    if ws is None:
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
-        _WORKSPACES[key] = ws
-    return ws
+    # One workspace per (device, op, dtype, batch, heads, head_dim). Its layout
+    # also depends on the context length, so a call with another length than
+    # the previous one zero-fills it first (enqueued on the current stream):
+    # a cache that grows by one position per step (transformers' DynamicCache)
+    # reuses one buffer, as the reference's buffer cache does once L >= 2N
+    # (triton_atopn.py:74-80), instead of keeping one per length.
+    key = (device.index, op, args.dtype, args.B, args.Hq, args.Hk, args.Hv, args.D)
+    ent = _WORKSPACES.get(key)
+    if ent is None or ent[0].numel() < nbytes:
+        size = nbytes if ent is None else max(nbytes, ent[0].numel() * 5 // 4)
+        ent = [torch.zeros(size, dtype=torch.uint8, device=device), args.L]
+        _WORKSPACES[key] = ent
+    elif ent[1] != args.L:
+        ent[0].zero_()
+        ent[1] = args.L
+    return ent[0]
 
 
 def _attn_args(q, k, v, attention_mask, scaling) -> L.SagaAttnArgs:

@@ -4,40 +4,44 @@ The attention function here is a CPU stand-in for the saga_b200 decode
 kernels. It consumes the decode token that SagaStaticCache recorded, writes
 it at the recorded device-side position itself, and runs SDPA. The test
 checks the cache class and the hand-off that the fused kernel relies on:
-logits and cache contents must equal a run with transformers' own
-StaticCache.
+logits and cache contents must equal a run with the reference's StaticCache
+(keys merged to one head, values with the config's heads).
 """
 import pytest
 import torch
 
 transformers = pytest.importorskip("transformers")
-from transformers import AttentionInterface, LlamaConfig, LlamaForCausalLM  # noqa: E402
+from transformers import AttentionInterface  # noqa: E402
 from transformers.cache_utils import StaticCache  # noqa: E402
-from transformers.integrations.sdpa_attention import sdpa_attention_forward  # noqa: E402
+from transformers.integrations.sdpa_attention import repeat_kv  # noqa: E402
 
 from saga_b200.attention.cache import SagaStaticCache, take_pending  # noqa: E402
+from _hf_models import surgery_static_cache, tiny_llama  # noqa: E402
+
+Hq, Hv, Hk, D = 4, 2, 1, 16
 
 
-def _stand_in(module, query, key, value, attention_mask, **kwargs):
+def _stand_in(module, query, key, value, attention_mask, scaling=None, **kwargs):
     pend = take_pending(key)
     if pend is not None:  # what the fused kernel does: write the token, then attend
         k_new, v_new, pos = pend
         key.index_copy_(2, pos, k_new)
         value.index_copy_(2, pos, v_new)
-    return sdpa_attention_forward(module, query, key, value, attention_mask, **kwargs)
+    k = repeat_kv(key, query.shape[1] // key.shape[1])
+    v = repeat_kv(value, query.shape[1] // value.shape[1])
+    mask = None if attention_mask is None else attention_mask[:, :, :, :k.shape[-2]]
+    out = torch.nn.functional.scaled_dot_product_attention(query, k, v, attn_mask=mask, scale=scaling,
+                                                           is_causal=mask is None and query.shape[2] > 1)
+    return out.transpose(1, 2).contiguous(), None
 
 
 AttentionInterface.register("saga_cpu_stand_in", _stand_in)
 
 
-def _decode(cache_cls, steps=5):
-    torch.manual_seed(0)
-    cfg = LlamaConfig(vocab_size=128, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
-                      num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=256)
-    cfg._attn_implementation = "saga_cpu_stand_in"
-    model = LlamaForCausalLM(cfg).eval()
-    cache = cache_cls(config=cfg, max_cache_len=64)
-    prompt = torch.randint(0, 128, (2, 7))
+def _decode(make_cache, steps=5):
+    cfg, model = tiny_llama("cpu", "saga_cpu_stand_in", torch.float32, Hq=Hq, Hv=Hv, Hk=Hk, D=D, vocab=128)
+    cache = make_cache(cfg)
+    prompt = torch.randint(0, 128, (2, 7), generator=torch.Generator().manual_seed(1))
     logits = []
     with torch.no_grad():
         out = model(input_ids=prompt, past_key_values=cache, use_cache=True, cache_position=torch.arange(7))
@@ -51,19 +55,31 @@ def _decode(cache_cls, steps=5):
 
 
 def test_saga_static_cache_matches_static_cache():
-    ref, ref_cache = _decode(StaticCache)
-    got, cache = _decode(SagaStaticCache)
+    ref, ref_cache = _decode(lambda cfg: surgery_static_cache(cfg, 64, 2, Hk, Hv, "cpu", torch.float32))
+    got, cache = _decode(lambda cfg: SagaStaticCache(config=cfg, max_cache_len=64))
     assert torch.equal(got, ref)
     for a, b in zip(cache.layers, ref_cache.layers):
+        assert a.keys.shape[1] == Hk and a.values.shape[1] == Hv
         assert torch.equal(a.keys, b.keys) and torch.equal(a.values, b.values)
 
 
 def test_unconsumed_token_raises():
-    cfg = LlamaConfig(vocab_size=32, hidden_size=32, intermediate_size=64, num_hidden_layers=1,
-                      num_attention_heads=2, num_key_value_heads=1, head_dim=16)
+    cfg, _ = tiny_llama("cpu", "saga_cpu_stand_in", torch.float32, Hq=2, Hv=1, Hk=1, D=16, layers=1, vocab=32)
     cache = SagaStaticCache(config=cfg, max_cache_len=16)
     k = torch.zeros(1, 1, 1, 16)
     cache.layers[0].update(k, k)
     with pytest.raises(RuntimeError):
         cache.layers[0].update(k, k)
     take_pending(cache.layers[0].keys)
+
+
+def test_plain_static_cache_sizes_values_by_key_heads():
+    """Why the reference rebuilds its cache: transformers' own StaticLayer
+    gives the values the key-head count."""
+    cfg, _ = tiny_llama("cpu", "saga_cpu_stand_in", torch.float32, Hq=Hq, Hv=Hv, Hk=Hk, D=D, layers=1, vocab=32)
+    plain = StaticCache(config=cfg, max_cache_len=8)
+    plain.layers[0].lazy_initialization(torch.zeros(1, Hk, 1, D), torch.zeros(1, Hv, 1, D))
+    assert plain.layers[0].values.shape[1] == Hk
+    ours = SagaStaticCache(config=cfg, max_cache_len=8)
+    ours.layers[0].lazy_initialization(torch.zeros(1, Hk, 1, D), torch.zeros(1, Hv, 1, D))
+    assert ours.layers[0].values.shape[1] == Hv
