@@ -856,6 +856,15 @@ __device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc
   return weight_from_logit<T, MODE>(Num<T>::to_f(sc[i * SH + hl]), misc, hl);
 }
 
+constexpr int kSlotS = 0, kSlotCnt = 1, kSlotM = 2, kSlotL = 3, kSlotO = 4;
+// Slot k of head hl inside one record of G * (D + 4) slots: the scalar fields
+// of every head first ([field][head]), then the partial outputs ([head][d]).
+// An exchange of one field over the heads, and a merge slice of consecutive
+// outputs of one chunk, then read consecutive slots (a few cache lines per
+// warp instead of one per lane).
+__device__ __forceinline__ size_t slot_in_record(int G, int D, int hl, int k) {
+  return k < kSlotO ? (size_t)k * G + hl : (size_t)kSlotO * G + (size_t)hl * D + (k - kSlotO);
+}
 // Slot address: group g, chunk c, local head hl, field k.
 template <bool SHD>
 __device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, int g, int c, int hl, int k) {
@@ -864,15 +873,14 @@ __device__ __forceinline__ unsigned long long* slot_at(const DecodeParams& p, in
     owner = c / p.c_local;
     c -= owner * p.c_local;
   }
-  return p.slot_base[owner] + (((size_t)g * p.c_local + c) * p.G + hl) * (size_t)(p.D + 4) + k;
+  return p.slot_base[owner] + ((size_t)g * p.c_local + c) * p.G * (size_t)(p.D + 4) + slot_in_record(p.G, p.D, hl, k);
 }
-constexpr int kSlotS = 0, kSlotCnt = 1, kSlotM = 2, kSlotL = 3, kSlotO = 4;
 
 // Sequence sharding: the combined value of device s's chunks, in device s's
-// workspace past the chunk slots: [group][head][D + 4].
+// workspace past the chunk slots: one record of G * (D + 4) per group.
 __device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p, int g, int s, int hl, int k) {
   const size_t chunk_slots = (size_t)p.B * p.Hk * p.c_local * p.G * (p.D + 4);
-  return p.slot_base[s] + chunk_slots + ((size_t)g * p.G + hl) * (size_t)(p.D + 4) + k;
+  return p.slot_base[s] + chunk_slots + (size_t)g * p.G * (p.D + 4) + slot_in_record(p.G, p.D, hl, k);
 }
 
 // ---------------------------------------------------------------------------
@@ -1497,32 +1505,36 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
 // one burst; sums run in chunk order.
 // ---------------------------------------------------------------------------
 // One merge level for outputs [lo, lo + nout) (heads hl0 .. hl0 + nhs - 1):
-// from nsrc partials (m, l per head; o per output) at src(k, hl, field),
-// misc->lsum[hh] = l and misc->aux2[hh] = m of the combination, and
+// from nsrc partials, each a slot record at rec(k) (m, l per head; o per
+// output), misc->lsum[hh] = l and misc->aux2[hh] = m of the combination, and
 // emit(k, o, hh) for every output with o relative to that m. The
-// combination order is fixed.
-template <int D, int MODE, bool SHD, typename Src, typename Emit>
-__device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, int nout, int hl0, int nhs, uint32_t tag,
+// combination order is fixed. A record's partial outputs are [head][d], so
+// the slice of source k is one run of consecutive slots from
+// rec(k) + kSlotO * G + lo.
+template <int D, int MODE, bool SHD, typename Rec, typename Emit>
+__device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, int nout, int hl0, int nhs, uint32_t tag,
                             uint8_t* scratch, Emit emit, Misc* misc, bool final_level) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t* ml = reinterpret_cast<uint32_t*>(scratch);  // [nhs][nsrc][2]
-  uint32_t* ov = ml + nhs * nsrc * 2;                   // [nout][nsrc]
+  uint32_t* ov = ml + nhs * nsrc * 2;                   // [nsrc][nout]
   const int n_ml = nhs * nsrc * 2;
-  const FastDiv div2c((uint32_t)(2 * nsrc)), divc((uint32_t)nsrc);
+  const int G = p.G;
+  const FastDiv div2c((uint32_t)(2 * nsrc)), divn((uint32_t)nout);
   slots_gather<SHD>(
       n_ml + nout * nsrc,
       [&](int i) {
         if (i < n_ml) {
           const int hh = (int)div2c.div((uint32_t)i), r = i - hh * 2 * nsrc;
-          return src(r >> 1, hl0 + hh, kSlotM + (r & 1));
+          return rec(r >> 1) + (kSlotM + (r & 1)) * G + hl0 + hh;
         }
         const int k = i - n_ml;
-        const int kq = (int)divc.div((uint32_t)k);
-        const int o = lo + kq;
-        return src(k - kq * nsrc, o / D, kSlotO + o % D);
+        const int c = (int)divn.div((uint32_t)k);
+        return rec(c) + (kSlotO * G + lo + (k - c * nout));
       },
       tag, ml, p.status);
+  trace_sub(p, 25);
   __syncthreads();
+  trace_sub(p, 26);
   float* scl = reinterpret_cast<float*>(ov + nout * nsrc);  // [nhs][nsrc]
   for (int hh = warp; hh < nhs; hh += kWarps) {
     float M = -INFINITY;
@@ -1548,7 +1560,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Src src, int lo, in
   for (int k = threadIdx.x; k < nout; k += kThreads) {
     const int hh = (lo + k) / D - hl0;
     float a = 0.f;
-    for (int c = 0; c < nsrc; ++c) a += __uint_as_float(ov[k * nsrc + c]) * scl[hh * nsrc + c];
+    for (int c = 0; c < nsrc; ++c) a += __uint_as_float(ov[c * nout + k]) * scl[hh * nsrc + c];
     emit(k, a, hh);
   }
 }
@@ -1579,7 +1591,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
   };
   if constexpr (!SHD) {
     merge_level<D, MODE, false>(
-        p, p.c_local, [&](int c, int hl, int f) { return slot_at<false>(p, g, c, hl, f); }, lo, nout, hl0, nhs, tag,
+        p, p.c_local, [&](int c) { return slot_at<false>(p, g, c, 0, 0); }, lo, nout, hl0, nhs, tag,
         scratch, write_out, misc, true);
     if (threadIdx.x == 0) trace_stamp(p, 15);
   } else {
@@ -1589,7 +1601,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
       slot_put<true>(shard_slot(p, g, p.shard, o / D, kSlotO + o % D), tag, __float_as_uint(a));
     };
     merge_level<D, MODE, true>(
-        p, p.c_local, [&](int c, int hl, int f) { return slot_at<true>(p, g, c0 + c, hl, f); }, lo, nout, hl0, nhs,
+        p, p.c_local, [&](int c) { return slot_at<true>(p, g, c0 + c, 0, 0); }, lo, nout, hl0, nhs,
         tag, scratch, publish, misc, false);
     for (int hh = threadIdx.x; hh < nhs; hh += kThreads) {
       slot_put<true>(shard_slot(p, g, p.shard, hl0 + hh, kSlotM), tag, __float_as_uint(misc->aux2[hh]));
@@ -1599,7 +1611,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
     if (threadIdx.x == 0) trace_stamp(p, 15);
     // every device's partial of the same slice
     merge_level<D, MODE, true>(
-        p, p.shards, [&](int sh, int hl, int f) { return shard_slot(p, g, sh, hl, f); }, lo, nout, hl0, nhs, tag,
+        p, p.shards, [&](int sh) { return shard_slot(p, g, sh, 0, 0); }, lo, nout, hl0, nhs, tag,
         scratch, write_out, misc, true);
   }
   trace_sub(p, 21);
@@ -2104,6 +2116,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     __syncthreads();
 
     // ---- merge of the group's partials, split across its chunks
+    trace_sub(p, 24);
     merge_slice<T, D, MODE, SHD>(p, g, jl, b, h0, work, misc);
     SAGA_TRACE(6)
 
