@@ -56,6 +56,7 @@ typedef enum {
 #define SAGA_STATUS_OVERFLOW 0x4       /* some row had more than K passing positions */
 #define SAGA_STATUS_EMPTY_ROW 0x8      /* some row selected nothing (output is NaN) */
 #define SAGA_STATUS_APPEND_RANGE 0x10  /* append_pos_dev held a position outside [0, L): no append */
+#define SAGA_STATUS_PAGE_RANGE 0x20    /* a page table entry outside [0, num_pages): page 0 was read */
 
 /* Descriptor shared by the attention entry points. Unused fields are ignored.
  * Strides are in elements. */
@@ -129,6 +130,24 @@ typedef struct SagaAttnArgs {
    * the append at a position that advances (an HF static cache's length).
    * Not with shards > 1. */
   const int64_t* append_pos_dev;
+
+  /* Optional paged caches (no counterpart in the reference, whose caches are
+   * contiguous [B, H, L, D] tensors; it copies a prefilled cache per batch
+   * row, speedup.py:155-160). With page_table non-NULL, k and v point at page
+   * pools [num_pages][H][page_len][D]: k_sb / v_sb are the page strides, and
+   * k_sh, k_sl / v_sh, v_sl the head and row strides inside a page (elements).
+   * Logical position pos of sequence b lives in page
+   * page_table[b * pt_sb + pos / page_len]; rows of several sequences may
+   * share a page, but an appended row must go to a page of its own sequence.
+   * page_len is a power of two and a multiple of 128; L is the logical
+   * context length (<= pt_sb * page_len). A page number outside
+   * [0, num_pages) sets SAGA_STATUS_PAGE_RANGE and page 0 is read instead.
+   * saga_atopn_decode, saga_atopn_calibrate, saga_dense_decode and
+   * saga_attn_logits only; not with shards > 1. */
+  const int32_t* page_table;
+  int64_t pt_sb;
+  int32_t page_len;
+  int32_t num_pages;
 } SagaAttnArgs;
 
 /* Ops understood by saga_workspace_bytes. */

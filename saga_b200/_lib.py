@@ -20,6 +20,7 @@ STATUS_NONFINITE_THR = 0x2
 STATUS_OVERFLOW = 0x4
 STATUS_EMPTY_ROW = 0x8
 STATUS_APPEND_RANGE = 0x10
+STATUS_PAGE_RANGE = 0x20
 
 _i32, _i64, _f32, _vp, _sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -45,6 +46,7 @@ class SagaAttnArgs(ctypes.Structure):
         ("nsel", _i32), ("pos_offset", _i32), ("shards", _i32), ("shard", _i32),
         ("shard_workspaces", _vp * 8),
         ("append_pos_dev", _vp),
+        ("page_table", _vp), ("pt_sb", _i64), ("page_len", _i32), ("num_pages", _i32),
     ]
 
 

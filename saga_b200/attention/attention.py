@@ -77,7 +77,8 @@ def _mask(attention_mask, key):
 # =============================================================================
 
 def _pending(key):
-    """Decode token recorded by SagaStaticCache for this key cache (or None)."""
+    """Decode token recorded by SagaStaticCache / SagaPagedCache for this key
+    cache (or None)."""
     try:
         from .cache import take_pending
     except Exception:  # pragma: no cover - transformers missing
@@ -85,10 +86,30 @@ def _pending(key):
     return take_pending(key)
 
 
+def _paged(key, attention_mask):
+    """For the key view of a SagaPagedCache decode step: the key and value
+    pools, the mask, and the keyword arguments of the paged fused call
+    (decode token, page table, logical length); else None."""
+    try:
+        from .cache import take_paged
+    except Exception:  # pragma: no cover - transformers missing
+        return None
+    pg = take_paged(key)
+    if pg is None:
+        return None
+    kpool, vpool, table, ctx = pg
+    k_new, v_new, pos = _pending(key)
+    mask = None if attention_mask is None else attention_mask[:, :, :, :ctx]
+    return kpool, vpool, mask, dict(k_new=k_new, v_new=v_new, append_pos=pos, page_table=table, context_len=ctx)
+
+
 def full_einsum_forward(query, key, value, attention_mask=None, is_causal=False, scaling=None):
     """Dense GQA decode with asymmetric key/value head counts -> [B, Hq, 1, D]."""
     if query.shape[2] != 1:
         raise NotImplementedError("saga_b200 full_einsum_forward serves decode (one query position)")
+    pg = _paged(key, attention_mask)
+    if pg is not None:
+        return _ops.dense_decode(query, pg[0], pg[1], pg[2], _ops.scaling_or_default(query, scaling), **pg[3])
     pend = _pending(key)
     if pend is not None:
         return torch.ops.saga.dense_decode_append(query, key, value, _mask(attention_mask, key),
@@ -163,6 +184,10 @@ def approx_top_n_attention_amortized_cal(query, key, value, attention_mask=None,
     AMORTIZED_THRESHOLD_TENSOR[layer_idx]."""
     b, q_h, l_q, d = query.shape
     thr = _threshold_row(layer_idx, b * q_h)
+    pg = _paged(key, attention_mask)
+    if pg is not None:
+        return _ops.atopn_calibrate(query, pg[0], pg[1], pg[2], thr, int(top_n_attention),
+                                    _ops.scaling_or_default(query, scaling), **pg[3])
     pend = _pending(key)
     if pend is not None:
         return torch.ops.saga.atopn_calibrate_append(query, key, value, _mask(attention_mask, key), thr,
@@ -177,6 +202,10 @@ def approx_top_n_attention_amortized(query, key, value, attention_mask=None, is_
     """Later decode steps (attention.py:192-209): cached thresholds, one fused kernel."""
     b, q_h, l_q, d = query.shape
     thr = _threshold_row(layer_idx, b * q_h)
+    pg = _paged(key, attention_mask)
+    if pg is not None:
+        return _ops.atopn_decode(query, pg[0], pg[1], pg[2], thr, int(top_n_attention),
+                                 _ops.scaling_or_default(query, scaling), **pg[3])
     pend = _pending(key)
     if pend is not None:
         return torch.ops.saga.atopn_decode_append(query, key, value, _mask(attention_mask, key), thr,

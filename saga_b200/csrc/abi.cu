@@ -45,6 +45,18 @@ int check_shapes(const SagaAttnArgs* a) {
     return fail(SAGA_ERR_UNSUPPORTED, "mask must be bool or the logits dtype");
   if (!(a->scaling == a->scaling)) return fail(SAGA_ERR_INVALID, "scaling is NaN");
   if (a->top_n < 0) return fail(SAGA_ERR_INVALID, "top_n must not be negative");
+  if (a->page_table) {
+    if (a->page_len < 128 || (a->page_len & (a->page_len - 1)))
+      return fail(SAGA_ERR_INVALID, "page_len must be a power of two and at least 128");
+    if (a->num_pages <= 0) return fail(SAGA_ERR_INVALID, "num_pages must be positive");
+    if (a->pt_sb <= 0 || a->pt_sb * (int64_t)a->page_len < a->L)
+      return fail(SAGA_ERR_INVALID, "page table rows must cover L positions (pt_sb * page_len >= L)");
+    // a head's rows inside a page must not run into the next head's
+    if ((a->Hk > 1 && (int64_t)(a->page_len - 1) * a->k_sl + a->D > a->k_sh) ||
+        (a->Hv > 1 && (int64_t)(a->page_len - 1) * a->v_sl + a->D > a->v_sh))
+      return fail(SAGA_ERR_INVALID, "a page's rows of one head overlap the next head");
+    if (a->shards > 1) return fail(SAGA_ERR_UNSUPPORTED, "paged caches are not supported with sequence sharding");
+  }
   return SAGA_OK;
 }
 
@@ -55,6 +67,7 @@ int check_attn(const SagaAttnArgs* a, int op) {
   if (!a->q || !a->k || !a->v) return fail(SAGA_ERR_INVALID, "q, k and v must be non-NULL");
   if (!aligned(a->k, 16) || !aligned(a->v, 16))
     return fail(SAGA_ERR_INVALID, "key and value caches must be 16-byte aligned");
+  if (a->page_table && !aligned(a->page_table, 4)) return fail(SAGA_ERR_INVALID, "page_table must be 4-byte aligned");
   if (op == SAGA_OP_LOGITS) {
     if (!a->logits_out || a->lo_ld < a->L) return fail(SAGA_ERR_INVALID, "logits_out [R, >=L] required");
     return SAGA_OK;

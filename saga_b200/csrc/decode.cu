@@ -242,6 +242,12 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
   p.v_new = a->v_new; p.vn_sb = a->vn_sb; p.vn_sh = a->vn_sh;
   p.append_pos = a->append_pos;
   p.append_pos_dev = reinterpret_cast<const long long*>(a->append_pos_dev);
+  p.page_table = a->page_table;
+  p.pt_sb = a->pt_sb;
+  p.page_len = a->page_table ? a->page_len : 0;
+  p.page_shift = 0;
+  while (p.page_len > 0 && (1 << p.page_shift) < p.page_len) ++p.page_shift;
+  p.num_pages = a->page_table ? a->num_pages : 0;
   p.logit_thr_out = a->logit_thr_out; p.count_out = a->count_out;
   p.sel_idx_out = a->sel_idx_out; p.sel_ld = a->sel_ld;
   p.logits_out = a->logits_out; p.lo_ld = a->lo_ld;
@@ -275,10 +281,14 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     }
     const uint64_t es = 2;
     // strides of size-1 dims do not matter; keep them valid (multiples of 16 B)
+    // contiguous: {D, L, Hk, B}; paged: {D, page_len, Hk, num_pages} over the pool
+    const bool paged = a->page_table != nullptr;
+    const uint64_t rows = paged ? (uint64_t)a->page_len : (uint64_t)a->L;
+    const uint64_t outer = paged ? (uint64_t)a->num_pages : (uint64_t)a->B;
     const uint64_t sl = (uint64_t)a->k_sl * es;
-    const uint64_t sh = a->Hk > 1 ? (uint64_t)a->k_sh * es : sl * (uint64_t)a->L;
-    const uint64_t sb = a->B > 1 ? (uint64_t)a->k_sb * es : sh * (uint64_t)a->Hk;
-    cuuint64_t dims[4] = {(cuuint64_t)a->D, (cuuint64_t)a->L, (cuuint64_t)a->Hk, (cuuint64_t)a->B};
+    const uint64_t sh = a->Hk > 1 ? (uint64_t)a->k_sh * es : sl * rows;
+    const uint64_t sb = outer > 1 ? (uint64_t)a->k_sb * es : sh * (uint64_t)a->Hk;
+    cuuint64_t dims[4] = {(cuuint64_t)a->D, (cuuint64_t)rows, (cuuint64_t)a->Hk, (cuuint64_t)outer};
     cuuint64_t strides[3] = {sl, sh, sb};
     cuuint32_t box[4] = {64, 128, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};

@@ -34,7 +34,7 @@ constexpr int kMaxShards = 8;   // devices a sequence can be sharded over
 
 // Shared-memory carve of the fused kernel, in bytes from a 1024-aligned base.
 struct SmemLayout {
-  int misc, qop, scores, tail, sel, eq, hmask, list, wbuf, work, xbuf, total;
+  int misc, qop, scores, tail, sel, eq, hmask, list, wbuf, work, xbuf, tpg, total;
   int work_bytes;  // K-tile ring / SIMT stages, then V rows, histograms, reductions
   int br;          // value rows per gather batch (CUDA-core P.V)
   int brw;         // value-row slots per pass of the tensor-core P.V (multiple of 16; 0 = not used)
@@ -94,6 +94,7 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   } else {     // fp32 weights [br][8], then the cross-warp reduction buffer
     l.wbuf = off;  off += align_up(br * 8 * 4, 128) + align_up(8 * (D + 1) * 4, 128);
   }
+  l.tpg = off;    off += align_up(4 * (CL / 128), 128);  // paged caches: page of each 128-row tile of the chunk
   l.total = off + 1024;  // slack to align the dynamic base to 1024
   l.work_bytes = work;
   l.br = br;
@@ -117,6 +118,10 @@ struct DecodeParams {
   const void* v_new; int64_t vn_sb, vn_sh;
   int append_pos;
   const long long* append_pos_dev;  // when set, the append position is read from here
+  // paged caches: pools [num_pages][H][page_len][D], k_sb / v_sb the page strides
+  const int* page_table;  // [B][pt_sb] page numbers, or null (contiguous caches)
+  long long pt_sb;
+  int page_len, page_shift, num_pages;
   float* logit_thr_out; int* count_out; int* sel_idx_out; int sel_ld;
   void* logits_out; int64_t lo_ld;
   int* ctrl; ChunkStat* stats; int* hist;

@@ -92,6 +92,50 @@ struct Misc {
 };
 static_assert(sizeof(Misc) <= 6144, "Misc must fit its 6 KB slot");
 
+// Paged caches: the page holding logical position pos of sequence b. A page
+// number outside the pool sets SAGA_STATUS_PAGE_RANGE and page 0 is read.
+__device__ __forceinline__ int page_of(const DecodeParams& p, int b, int pos) {
+  int pg = __ldg(p.page_table + (int64_t)b * p.pt_sb + (pos >> p.page_shift));
+  if ((unsigned)pg >= (unsigned)p.num_pages) {
+    set_status(p.status, SAGA_STATUS_PAGE_RANGE);
+    pg = 0;
+  }
+  return pg;
+}
+// Element offset of the row of (sequence b, head h, position pos) in a cache
+// with strides (sb, sh, sl): contiguous, or inside page pg of a pool, sb then
+// being the page stride.
+__device__ __forceinline__ int64_t cache_row(const DecodeParams& p, int64_t sb, int64_t sh, int64_t sl, int b, int h,
+                                             int pos, int pg) {
+  return p.page_table ? (int64_t)pg * sb + (int64_t)h * sh + (int64_t)(pos & (p.page_len - 1)) * sl
+                      : (int64_t)b * sb + (int64_t)h * sh + (int64_t)pos * sl;
+}
+// Page of every 128-row tile of the item's chunk (paged caches), filled at
+// item start; it sits in the same shared-memory carve as misc.
+__device__ __forceinline__ int* tile_pages(const DecodeParams& p, const Misc* misc) {
+  return reinterpret_cast<int*>(const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(misc)) - p.sm.misc + p.sm.tpg);
+}
+// TMA coordinates (row, outer) of the key tile at logical row y of sequence
+// b: {y, b} for a contiguous cache; {row in page, page} for a paged one,
+// own tile t >= 0 from the chunk's tile pages, a tail tile (t < 0) from the
+// page table.
+__device__ __forceinline__ void k_tile_coords(const DecodeParams& p, const Misc* misc, int b, int y, int t, int* ty,
+                                              int* tw) {
+  if (!p.page_table) {
+    *ty = y;
+    *tw = b;
+    return;
+  }
+  *tw = t >= 0 ? tile_pages(p, misc)[t] : page_of(p, b, y);
+  *ty = y & (p.page_len - 1);
+}
+// Element offset of the value row of head vh at chunk position r (chunks
+// start on a tile boundary, so a tile lies in one page).
+__device__ __forceinline__ int64_t value_row(const DecodeParams& p, const Misc* misc, int b, int vh, int p0, int r) {
+  return p.page_table ? cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, tile_pages(p, misc)[r >> 7])
+                      : cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, 0);
+}
+
 template <int MODE>
 __device__ __forceinline__ void item_prologue(const DecodeParams& p, int b, int kh, Misc* misc);
 
@@ -334,7 +378,11 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
     for (int c = threadIdx.x; c < SUB * CPR; c += kThreads) {
       const int r = c / CPR, cc = c % CPR;
       const bool ok = (s * SUB + r) < cnt;
-      const T* src = kbase + (int64_t)(ok ? (a + s * SUB + r) : a) * p.k_sl + cc * (16 / (int)sizeof(T));
+      const int pos = ok ? (a + s * SUB + r) : a;
+      const T* src = p.page_table ? reinterpret_cast<const T*>(p.k) +
+                                        cache_row(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, page_of(p, b, pos)) +
+                                        cc * (16 / (int)sizeof(T))
+                                  : kbase + (int64_t)pos * p.k_sl + cc * (16 / (int)sizeof(T));
       cp_async16(buf + r * PITCH + cc * 16, src, ok);
     }
     cp_async_commit();
@@ -435,11 +483,13 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         break;
       }
       const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
+      int ty, tw;
+      k_tile_coords(p, misc, b, y, q - n_pre, &ty, &tw);
       mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
       uint8_t* dst = ring + rg.ps * TILE_BYTES;
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb)
-        tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
+        tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, ty, kh, tw, &misc->full[rg.ps]);
       if (q < 16) trace_col(p, 16 + q, clock64());
       ++pre_issued;
       if (++rg.ps == (uint32_t)NS) {
@@ -475,11 +525,13 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
           break;
         }
         const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
+        int ty, tw;
+        k_tile_coords(p, misc, b, y, q - n_pre, &ty, &tw);
         mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
         uint8_t* dst = ring + rg.ps * TILE_BYTES;
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb)
-          tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, y, kh, b, &misc->full[rg.ps]);
+          tma_load_4d(dst + kb * 16384, &p.tmap, kb * 64, ty, kh, tw, &misc->full[rg.ps]);
         ++issued;
         if (q < 16) trace_col(p, 16 + q, clock64());
         if (++rg.ps == (uint32_t)NS) {
@@ -904,9 +956,8 @@ __device__ __forceinline__ void issue_rows(const DecodeParams& p, int b, int p0,
     const int r = i / CPR, c = i % CPR;
     const uint32_t ent = list[e0 + r];
     const int vh = misc->gvh[ent >> 24];
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.v) + (int64_t)b * p.v_sb +
-                                                          (int64_t)vh * p.v_sh +
-                                                          (int64_t)(p0 + (int)(ent & 0xFFFFu)) * p.v_sl);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.v) +
+                                                          value_row(p, misc, b, vh, p0, (int)(ent & 0xFFFFu)));
     cp_async16(work + (size_t)r * ROWB + c * 16, src + c * 16, true);
   }
   cp_async_commit();
@@ -947,6 +998,20 @@ __device__ __noinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0,
     if (a >= z) continue;
     const int e0 = misc->gstart[gi], rows = misc->gstart[gi + 1] - e0, gbase = misc->gpad[gi];
     const T* vg = vb + (int64_t)misc->gvh[gi] * p.v_sh;
+    if (p.page_table) {  // paged: each row's page from the chunk's tile pages
+      const T* v0 = reinterpret_cast<const T*>(p.v);
+      for (int s = a + warp * 2 + sub; s < z; s += kWarps * 2) {
+        const int r = s - gbase;
+        uint8_t* dst = work + pv_row_off(s - pbase, sg);
+        if (r < rows) {
+          const int pos = (int)(list[e0 + r] & 0xFFFFu);
+          cp_async16(dst, v0 + value_row(p, misc, b, misc->gvh[gi], p0, pos) + sg * 8, true);
+        } else {
+          cp_async16(dst, v0, false);
+        }
+      }
+      continue;
+    }
 #pragma unroll 2
     for (int s = a + warp * 2 + sub; s < z; s += kWarps * 2) {
       const int r = s - gbase;
@@ -1266,7 +1331,9 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
 #pragma unroll 2
     for (int e = warp * RPI + sub; e < carry; e += kWarps * RPI) {
       const uint32_t ent = list[e];
-      const T* src = vb + (int64_t)misc->gvh[ent >> 24] * p.v_sh + (int64_t)(ent & 0xFFFFu) * p.v_sl;
+      const T* src = p.page_table ? reinterpret_cast<const T*>(p.v) +
+                                        value_row(p, misc, b, misc->gvh[ent >> 24], p0, (int)(ent & 0xFFFFu))
+                                  : vb + (int64_t)misc->gvh[ent >> 24] * p.v_sh + (int64_t)(ent & 0xFFFFu) * p.v_sl;
       cp_async16(work + (size_t)e * ROWB + seg * 16, reinterpret_cast<const uint8_t*>(src) + seg * 16, true);
     }
   }
@@ -1731,6 +1798,13 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       if (warp == 3) item_prologue<MODE>(p, b, kh, misc);
     }
 
+    // ---- paged caches: the page of each of the chunk's tiles (read by the
+    // scorer's TMA and by the value-row gathers after the next barrier)
+    if (p.page_table) {
+      int* tpg = tile_pages(p, misc);
+      for (int t = threadIdx.x; t < (n + 127) / 128; t += kThreads) tpg[t] = page_of(p, b, p0 + t * 128);
+    }
+
     // ---- fused append of the decode token (StaticLayer.update's index_copy_).
     // Every chunk of the group writes the new key row (the same values) before
     // it reads the cache, because every chunk scores the tail positions; the
@@ -1744,16 +1818,15 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     if (p.k_new && apos >= 0) {
       const int pos = apos;
       const T* src = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.kn_sb + (int64_t)kh * p.kn_sh;
-      T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + (int64_t)b * p.k_sb + (int64_t)kh * p.k_sh +
-               (int64_t)pos * p.k_sl;
+      const int apg = p.page_table ? page_of(p, b, pos) : 0;  // an append goes to a page of its own sequence
+      T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + cache_row(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, apg);
       for (int d = threadIdx.x; d < D; d += kThreads) dst[d] = src[d];
       if (p.v_new && pos >= p0 && pos < p0 + n) {
         const int vh_lo = h0 / p.Gv, vh_hi = (h0 + G - 1) / p.Gv;
         for (int i = threadIdx.x; i < (vh_hi - vh_lo + 1) * D; i += kThreads) {
           const int vh = vh_lo + i / D, d = i % D;
           const T* vs = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.vn_sb + (int64_t)vh * p.vn_sh;
-          T* vd = const_cast<T*>(reinterpret_cast<const T*>(p.v)) + (int64_t)b * p.v_sb + (int64_t)vh * p.v_sh +
-                  (int64_t)pos * p.v_sl;
+          T* vd = const_cast<T*>(reinterpret_cast<const T*>(p.v)) + cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, pos, apg);
           vd[d] = vs[d];
         }
       }

@@ -97,17 +97,32 @@ def _workspace(args: L.SagaAttnArgs, op: int, device: torch.device) -> torch.Ten
     return ent[0]
 
 
-def _attn_args(q, k, v, attention_mask, scaling) -> L.SagaAttnArgs:
-    _require_cuda(q, k, v, attention_mask)
+def _attn_args(q, k, v, attention_mask, scaling, page_table=None, context_len=None) -> L.SagaAttnArgs:
+    """Kernel arguments. With ``page_table`` (int32 [B, max_pages] on the
+    device), ``k`` and ``v`` are page pools [pages, H, page_len, D] and
+    ``context_len`` is the logical length L of every sequence."""
+    _require_cuda(q, k, v, attention_mask, page_table)
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise ValueError("query, key and value must be 4-D [B, H, L, D]")
     B, Hq, Lq, D = q.shape
     if Lq != 1:
         raise ValueError(f"decode kernels take one query position (got {Lq})")
-    Hk, Lk = k.shape[1], k.shape[2]
-    Hv = v.shape[1]
-    if k.shape[0] != B or v.shape[0] != B or k.shape[3] != D or v.shape[3] != D or v.shape[2] != Lk:
-        raise ValueError("query/key/value shapes disagree")
+    Hk, Hv = k.shape[1], v.shape[1]
+    if page_table is None:
+        Lk = k.shape[2]
+        if k.shape[0] != B or v.shape[0] != B or k.shape[3] != D or v.shape[3] != D or v.shape[2] != Lk:
+            raise ValueError("query/key/value shapes disagree")
+    else:
+        page_len = k.shape[2]
+        if v.shape[2] != page_len or k.shape[3] != D or v.shape[3] != D:
+            raise ValueError("key/value page pools disagree with the query")
+        if page_table.dtype != torch.int32 or page_table.dim() != 2 or page_table.stride(1) != 1:
+            raise ValueError("page_table must be an int32 [B, max_pages] tensor with unit column stride")
+        if page_table.shape[0] < B:
+            raise ValueError("page_table has fewer rows than the batch")
+        if context_len is None or not 1 <= int(context_len) <= page_table.shape[1] * page_len:
+            raise ValueError("context_len in [1, max_pages * page_len] is required with a page table")
+        Lk = int(context_len)
     if k.dtype != q.dtype or v.dtype != q.dtype:
         raise TypeError("query, key and value must share a dtype")
     for name, t in (("query", q), ("key", k), ("value", v)):
@@ -133,6 +148,9 @@ def _attn_args(q, k, v, attention_mask, scaling) -> L.SagaAttnArgs:
         a.mask, a.m_sb, a.m_sh, a.m_sl = m.data_ptr(), m.stride(0), m.stride(1), m.stride(3)
     a.scaling = float(1.0 / math.sqrt(D) if scaling is None else scaling)
     a.append_pos = -1
+    if page_table is not None:
+        a.page_table, a.pt_sb = page_table.data_ptr(), page_table.stride(0)
+        a.page_len, a.num_pages = k.shape[2], min(k.shape[0], v.shape[0])
     return a
 
 
@@ -192,16 +210,18 @@ def _run(fn_name, a, op, device, diag=None):
 # ---------------------------------------------------------------------------
 
 def atopn_decode(query, key, value, attention_mask=None, threshold=None, top_n: int = 256,
-                 scaling=None, k_new=None, v_new=None, append_pos: int = -1, diag: Optional[dict] = None):
+                 scaling=None, k_new=None, v_new=None, append_pos: int = -1, diag: Optional[dict] = None,
+                 page_table=None, context_len=None):
     """Steady-state Atop-N step (attention.py:192-209) in one fused kernel.
 
     ``threshold`` holds the softmax-space threshold of each (batch, query head)
     row, e.g. ``AMORTIZED_THRESHOLD_TENSOR[layer, :B*Hq]``. With
     ``k_new``/``v_new`` the token is first written at ``append_pos`` of the
     caches. ``diag``, if a dict, receives per-row logit thresholds, passing
-    counts and the kept positions.
+    counts and the kept positions. With ``page_table``, key and value are
+    page pools (see ``_attn_args``).
     """
-    a = _attn_args(query, key, value, attention_mask, scaling)
+    a = _attn_args(query, key, value, attention_mask, scaling, page_table, context_len)
     if threshold is None or threshold.dtype != torch.float32 or not threshold.is_contiguous():
         raise ValueError("threshold must be a contiguous float32 tensor with B*Hq entries")
     if threshold.numel() < a.B * a.Hq:
@@ -217,11 +237,12 @@ def atopn_decode(query, key, value, attention_mask=None, threshold=None, top_n: 
 
 
 def atopn_calibrate(query, key, value, attention_mask=None, threshold_out=None, top_n: int = 256,
-                    scaling=None, k_new=None, v_new=None, append_pos: int = -1, diag: Optional[dict] = None):
+                    scaling=None, k_new=None, v_new=None, append_pos: int = -1, diag: Optional[dict] = None,
+                    page_table=None, context_len=None):
     """Calibration step (attention.py:173-189): writes the N-th largest
     probability of each row into ``threshold_out`` and returns the output of
     the renormalised top-N probabilities."""
-    a = _attn_args(query, key, value, attention_mask, scaling)
+    a = _attn_args(query, key, value, attention_mask, scaling, page_table, context_len)
     if threshold_out is None or threshold_out.dtype != torch.float32 or not threshold_out.is_contiguous():
         raise ValueError("threshold_out must be a contiguous float32 tensor with B*Hq entries")
     if threshold_out.numel() < a.B * a.Hq:
@@ -237,9 +258,9 @@ def atopn_calibrate(query, key, value, attention_mask=None, threshold_out=None, 
 
 
 def dense_decode(query, key, value, attention_mask=None, scaling=None, k_new=None, v_new=None,
-                 append_pos: int = -1, diag: Optional[dict] = None):
+                 append_pos: int = -1, diag: Optional[dict] = None, page_table=None, context_len=None):
     """Dense GQA decode (attention.py:64-85) for one query position."""
-    a = _attn_args(query, key, value, attention_mask, scaling)
+    a = _attn_args(query, key, value, attention_mask, scaling, page_table, context_len)
     _set_append(a, k_new, v_new, append_pos)
     out = _out_like(query)
     a.out, a.o_sb, a.o_sh = out.data_ptr(), out.stride(0), out.stride(1)

@@ -16,6 +16,9 @@ run the amortized kernel. Three runs of the same seeded model and prompt:
   further.
 All three must give the same logits and the same caches.
 
+SagaPagedCache: one prompt forked to several sequences that share its
+pages, against transformers' DynamicCache (which copies them).
+
 lm_eval_saga.py's flow (152-212): a DynamicCache that grows by one position
 per step, the threshold table created lazily with MAX_LAYERS rows, an exempt
 layer on the dense kernel, recalibration at the first step and every 32
@@ -244,3 +247,48 @@ def test_lm_eval_flow_dynamic_cache():
             ref = O.atopn_amortized(*args, c["thr"], TOP_N, "bf16", scaling=c["scaling"], mask=c["mask"])["out"]
         ok, stats = _out_close(c["out"].reshape(ref.shape), ref)
         assert ok, (c["kind"], c["layer"], c["step"], stats)
+
+
+# ---------------------------------------------------------------------------
+# SagaPagedCache: a prompt forked to several sequences that share its pages
+# ---------------------------------------------------------------------------
+
+def test_paged_cache_fork_matches_dynamic_cache():
+    """One prompt prefilled, forked to 4 sequences (transformers' DynamicCache
+    copies the tensors per sequence; SagaPagedCache shares the pages), then
+    the sequences decode different tokens across a page boundary. Same
+    kernels, same rows: identical logits."""
+    from transformers.cache_utils import DynamicCache
+    from saga_b200 import ops
+    from saga_b200 import _lib as Lb
+    from saga_b200.attention import attention as A
+    from saga_b200.attention.cache import SagaPagedCache
+    dev = torch.device("cuda", 0)
+    fork, prompt_len, steps = 4, 200, 70
+    cfg, model = tiny_llama(dev, "saga_hf_test", Hq=Hq, Hv=Hv, Hk=Hk)
+    prompt = torch.randint(0, cfg.vocab_size, (1, prompt_len), device=dev)
+
+    def run(cache):
+        A.init_amortized_threshold_tensor(dev, cfg.num_hidden_layers, fork * Hq)
+        logits = []
+        with torch.no_grad():
+            out = model(input_ids=prompt, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            cache.batch_repeat_interleave(fork)
+            tok = out.logits[:, -1].argmax(-1, keepdim=True).repeat(fork, 1)
+            tok = (tok + torch.arange(fork, device=dev).unsqueeze(1)) % cfg.vocab_size
+            for _ in range(steps):
+                out = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+                logits.append(out.logits[:, -1].float())
+                tok = out.logits[:, -1].argmax(-1, keepdim=True)
+        torch.cuda.synchronize()
+        return torch.stack(logits)
+
+    ops.read_status(dev)
+    ref = run(DynamicCache(config=cfg))
+    cache = SagaPagedCache(cfg, max_cache_len=512, page_len=128, num_pages=16)
+    got = run(cache)
+    assert torch.equal(got, ref), (got - ref).abs().max().item()
+    layer = cache.layers[0]
+    assert layer.length == prompt_len + steps and layer.batch == fork
+    assert layer.refs[layer.table_host[0][0]] == fork  # the prompt's full page is shared
+    assert ops.read_status(dev) & (Lb.STATUS_WAIT_TIMEOUT | Lb.STATUS_PAGE_RANGE) == 0
