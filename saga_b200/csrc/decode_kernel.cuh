@@ -1236,7 +1236,10 @@ __device__ __forceinline__ uint32_t task_occupancy(const uint32_t* __restrict__ 
   }
 }
 
-template <typename T, int D, int MODE>
+// TCPV: the kernel runs the tensor-core P.V (16-bit types at head_dim 128 on
+// the tensor-core scorer); otherwise the CUDA-core P.V's rows are issued here
+// when they fit one batch.
+template <typename T, int D, int MODE, bool TCPV>
 __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const T* __restrict__ sc,
                              const uint32_t* __restrict__ hmask, uint32_t* __restrict__ list, int* __restrict__ toff,
                              uint32_t* __restrict__ occ, uint8_t* __restrict__ work, uint8_t* __restrict__ wpv,
@@ -1298,7 +1301,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
   trace_sub(p, 4);
   for (int gi = threadIdx.x; gi <= ngroups; gi += kThreads) {
     misc->gstart[gi] = gi < ngroups ? toff[gi * nw] : carry;
-    if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
+    if constexpr (TCPV) {
       int s = 0;  // row slots of the groups before gi, each group padded to 16
       for (int k = 0; k < gi; ++k) {
         const int e1 = (k + 1 < ngroups) ? toff[(k + 1) * nw] : carry;
@@ -1309,13 +1312,13 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
   }
   __syncthreads();
   if (threadIdx.x == 0) trace_stamp(p, 5);
-  if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2 && MODE == MODE_AMORTIZED) {
+  if constexpr (TCPV && MODE == MODE_AMORTIZED) {
     // the first pass's weights before its row copies: the copies then do not
     // hold up these shared-memory reads
     pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), false);
     trace_sub(p, 5);
   }
-  if constexpr (uses_tc_pv(true, D) && sizeof(T) == 2) {
+  if constexpr (TCPV) {
     if (p.sm.brw > 0) {  // tensor-core P.V: the first pass's rows
       pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), 0);
       cp_async_commit();
@@ -1949,7 +1952,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       // lists, value-row copies and the first pass's weights go out while the
       // counts are exchanged
-      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
       slots_gather_field<SHD>(p, g, kSlotCnt, tag, xbuf);
       __syncthreads();
@@ -2174,13 +2177,13 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         hmask[i] = bits;
       }
       __syncthreads();
-      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
         gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else
         gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
-      gather_begin<T, D, MODE>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
         gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else

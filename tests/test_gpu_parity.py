@@ -279,3 +279,31 @@ def test_zero_threshold_table_overflows_to_lowest_k(gold):
     sel = diag["sel_idx"].cpu().numpy()
     assert np.all(sel[:, :kk] == np.arange(kk)[None, :])
     assert ops.read_status(_dev()) & 0x4
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("hq", [20, 32])
+def test_wide_groups_cuda_core_pv(dtype, hq):
+    """More than 16 query heads per key head: the CUDA-core scorer and P.V
+    (the tensor-core path takes G <= 16). Calibration, the amortized step
+    (on the calibrated thresholds) and dense decode against the oracle on
+    the same seeded inputs, with the tolerances above. The value rows fit
+    one gather batch here, the case whose rows were once never issued."""
+    from saga_b200 import ops
+    tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+    b, d, hk, hv, length, n = 2, 128, 1, 2, 1700, 64
+    g = torch.Generator(device=_dev()).manual_seed(21)
+    q = (torch.randn((b, hq, 1, d), generator=g, device=_dev()) * 0.5).to(tdt)
+    k = (torch.randn((b, hk, length, d), generator=g, device=_dev()) * 0.5).to(tdt)
+    v = (torch.randn((b, hv, length, d), generator=g, device=_dev()) * 0.5).to(tdt)
+    qn, kn, vn = (_np(x) for x in (q, k, v))
+    thr = torch.zeros(b * hq, dtype=torch.float32, device=_dev())
+    out = ops.atopn_calibrate(q, k, v, None, thr, n)
+    ref = O.atopn_calibrate(qn, kn, vn, n, dtype)
+    np.testing.assert_array_equal(_np(thr), ref["thr"])
+    assert _out_ok(_np(out).reshape(ref["out"].shape), ref["out"], dtype)
+    out = ops.atopn_decode(q, k, v, None, thr, n)
+    ref = O.atopn_amortized(qn, kn, vn, _np(thr), n, dtype)
+    assert _out_ok(_np(out).reshape(ref["out"].shape), ref["out"], dtype)
+    ref = O.dense_decode(qn, kn, vn, dtype)
+    assert _out_ok(_np(ops.dense_decode(q, k, v)).reshape(ref.shape), ref, dtype)
