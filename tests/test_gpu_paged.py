@@ -11,6 +11,8 @@ sequence uses, hold random values, which the kernels must never use. Cases:
   its own last page, against the contiguous caches copied per sequence as
   the reference's benchmark does (speedup.py:155-160);
 * the fused append of a decode token into each sequence's own last page;
+* D = 64, fp16, bool and additive masks, Hk = 2 with Hv = 4, and G = 32 (the
+  CUDA-core scorer);
 * a page number outside the pool: SAGA_STATUS_PAGE_RANGE, no fault (the
   kernel's own check reads page 0 instead).
 """
@@ -142,3 +144,32 @@ def test_page_number_outside_pool_sets_status():
     _status()
     ops.dense_decode(q, kp, vp, page_table=pt, context_len=600)
     assert _status() & Lb.STATUS_PAGE_RANGE
+
+
+@pytest.mark.parametrize("dtype,d,hq,hk,hv,mask_kind", [
+    (torch.bfloat16, 64, 8, 2, 4, "bool"),       # D = 64, two key heads, more value heads
+    (torch.float16, 128, 12, 1, 2, "additive"),  # fp16 with an additive mask
+    (torch.bfloat16, 128, 32, 1, 2, None),       # G = 32: CUDA-core scorer
+])
+def test_paged_configurations(dtype, d, hq, hk, hv, mask_kind):
+    """Other kernel configurations through the page table, against the
+    contiguous run (bit-exact), with masks read at logical positions."""
+    from saga_b200 import ops
+    b, length, n = 2, 1700, 64
+    g = torch.Generator(device=_dev()).manual_seed(21)
+    q = (torch.randn((b, hq, 1, d), generator=g, device=_dev()) * 0.5).to(dtype)
+    k = (torch.randn((b, hk, length, d), generator=g, device=_dev()) * 0.5).to(dtype)
+    v = (torch.randn((b, hv, length, d), generator=g, device=_dev()) * 0.5).to(dtype)
+    mask = None
+    if mask_kind == "bool":
+        mask = torch.rand((b, 1, 1, length), generator=g, device=_dev()) > 0.1
+    elif mask_kind == "additive":
+        mask = torch.where(torch.rand((b, hq, 1, length), generator=g, device=_dev()) > 0.1, 0.0, -1e4).to(dtype)
+    kp, vp, pt = _paginate((k, v), 256)
+    paged = dict(page_table=pt, context_len=length)
+    thr = torch.zeros(b * hq, dtype=torch.float32, device=_dev())
+    thr_p = torch.zeros_like(thr)
+    assert torch.equal(ops.atopn_calibrate(q, kp, vp, mask, thr_p, n, **paged), ops.atopn_calibrate(q, k, v, mask, thr, n))
+    assert torch.equal(thr_p, thr)
+    assert torch.equal(ops.atopn_decode(q, kp, vp, mask, thr, n, **paged), ops.atopn_decode(q, k, v, mask, thr, n))
+    assert torch.equal(ops.dense_decode(q, kp, vp, mask, **paged), ops.dense_decode(q, k, v, mask))
