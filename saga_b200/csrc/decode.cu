@@ -102,14 +102,15 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
   const int es = esize_of(a->dtype);
   const bool tc = (a->dtype != SAGA_FP32) && G <= 16;
   const int ngg = gather_groups_per_group(a->Hq, a->Hk, a->Hv);  // list rows per position
-  // tensor-core path: one CTA per SM, deepest K ring that fits; else two per SM
-  const int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
+  // tensor-core path: one CTA per SM, deepest K ring that fits; else two per
+  // SM, or one when not even a one-tile chunk fits half an SM's shared memory
+  int budget = tc ? di.smem_optin : std::min(di.smem_optin, 113 * 1024);
   // the exchanges stage every chunk of the group: with sequence sharding,
   // the other devices' chunks too
   const int shards = a->shards > 1 ? a->shards : 1;
   const int cbound = std::min(ntiles, 4096) * shards;
   const int target = tc ? di.sms : 2 * di.sms;
-  const int c_par = std::max(1, target / std::max(1, groups));
+  int c_par = std::max(1, target / std::max(1, groups));
   // Deepest K ring whose chunk still lets every group run in one wave; if no
   // ring depth allows that, the deepest one that fits.
   auto tiles_for = [&](int stages) {
@@ -121,6 +122,11 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
     return mt;
   };
   int ns = tc ? kMaxStages : 2, max_tiles = tiles_for(ns);
+  if (!tc && max_tiles == 0) {  // one CTA per SM: chunks for one wave of them
+    budget = di.smem_optin;
+    max_tiles = tiles_for(ns);
+    c_par = std::max(1, di.sms / std::max(1, groups));
+  }
   if (tc) {
     for (int s = kMaxStages; s >= 2; --s) {
       const int mt = tiles_for(s);

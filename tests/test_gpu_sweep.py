@@ -2,8 +2,7 @@
 
 dtype (bf16, fp16, fp32) x head_dim (64, 128) x head layouts (G = Hq / Hk
 from 1 to 32; Hv below, equal to and above Hk) x (batch, context, N, mask).
-That gives 141 seeded cases (fp32 with G = 32 at head_dim 128 is refused),
-each running the calibration step, the
+That gives 144 seeded cases, each running the calibration step, the
 amortized step on the calibrated thresholds, and dense decode. The golden
 fixtures pin the reference's own shapes; this sweep covers the kernel's other
 paths. These are the tensor-core and CUDA-core scorers, the tensor-core and
@@ -37,8 +36,6 @@ def _cases():
     for dt in ("bf16", "fp16", "fp32"):
         for d in (64, 128):
             for lay in LAYOUTS:
-                if dt == "fp32" and d == 128 and lay[0] // lay[1] > 20:
-                    continue  # refused: more shared memory than a CTA has (see test_refused_shape)
                 yield dt, d, lay
 
 
@@ -98,14 +95,19 @@ def test_configuration_against_oracle(dt, d, lay):
     assert ops.read_status(dev) & 0x1 == 0
 
 
-def test_refused_shape():
-    """fp32 with more than 16 query heads per key head at head_dim 128 needs
-    more shared memory than one CTA has: a clear error, no launch."""
+def test_wide_fp32_groups_use_the_whole_shared_memory():
+    """fp32 with G = 32 at head_dim 128 does not fit two CTAs per SM: the plan
+    falls back to one CTA per SM with all of its shared memory."""
     from saga_b200 import ops
-    from saga_b200 import _lib as Lb
     dev = torch.device("cuda", 0)
-    q = torch.zeros((1, 32, 1, 128), device=dev)
-    k = torch.zeros((1, 1, 300, 128), device=dev)
-    v = torch.zeros((1, 2, 300, 128), device=dev)
-    with pytest.raises(Lb.SagaError, match="shared memory"):
-        ops.dense_decode(q, k, v)
+    g = torch.Generator(device=dev).manual_seed(4)
+    q = torch.randn((2, 32, 1, 128), generator=g, device=dev) * 0.5
+    k = torch.randn((2, 1, 1700, 128), generator=g, device=dev) * 0.5
+    v = torch.randn((2, 2, 1700, 128), generator=g, device=dev) * 0.5
+    ref = O.dense_decode(*(x.cpu().numpy() for x in (q, k, v)), "fp32")
+    assert np.abs(ops.dense_decode(q, k, v).cpu().numpy() - ref).max() <= 1e-4
+    thr = torch.zeros(64, dtype=torch.float32, device=dev)
+    out = ops.atopn_calibrate(q, k, v, None, thr, 64)
+    rc = O.atopn_calibrate(*(x.cpu().numpy() for x in (q, k, v)), 64, "fp32")
+    assert np.abs(thr.cpu().numpy() - rc["thr"]).max() <= 1e-6
+    assert np.isfinite(out.cpu().numpy()).all()
