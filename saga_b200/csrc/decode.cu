@@ -1,6 +1,9 @@
 // Host side of the fused decode kernel: plan (chunking, shared-memory carve,
 // grid) and launch. The kernels are instantiated per dtype in decode_bf16.cu,
 // decode_fp16.cu and decode_fp32.cu (device code in decode_kernel.cuh).
+#include <array>
+#include <map>
+#include <mutex>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -89,7 +92,50 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
+// The kernel's dynamic shared-memory limit is a per-function, per-device
+// attribute; plans of different shapes may share a kernel, so it only rises.
+static int raise_smem_limit(const void* kfn, int smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> set_to;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  int& cur = set_to[{dev, kfn}];
+  if (smem <= cur) return 0;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
+  cur = smem;
+  return 0;
+}
+
+static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err);
+
+// Plans depend only on the device and the shapes, so they are computed once:
+// a decode step otherwise pays for the occupancy query and the attribute call
+// twice (workspace size, then launch).
 int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const std::array<long long, 12> key = {dev, mode, a->dtype, a->B, a->Hq, a->Hk, a->Hv, a->D, a->L, a->nsel,
+                                         a->shards, a->mask != nullptr};
+  static std::mutex mu;
+  static std::map<std::array<long long, 12>, DecodePlan> plans;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = plans.find(key);
+    if (it != plans.end()) {
+      *pl = it->second;
+      return SAGA_OK;
+    }
+  }
+  const int rc = compute_decode_plan(a, mode, pl, err);
+  if (rc == SAGA_OK) {
+    std::lock_guard<std::mutex> lock(mu);
+    plans[key] = *pl;
+  }
+  return rc;
+}
+
+static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err) {
   const DevInfo di = dev_info();
   if (di.sms <= 0) {
     *err = "no CUDA device";
@@ -180,7 +226,7 @@ int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::strin
     const int floor_smem = di.smem_per_sm / (max_per_sm + 1) + 1024;
     if (pl->smem < floor_smem) pl->smem = std::min(floor_smem, budget);
   }
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, pl->smem) != cudaSuccess) {
+  if (raise_smem_limit(kfn, pl->smem) != 0) {
     *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(cudaGetLastError());
     return SAGA_ERR_CUDA;
   }
@@ -298,13 +344,34 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     cuuint64_t strides[3] = {sl, sh, sb};
     cuuint32_t box[4] = {64, 128, 1, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = enc(&p.tmap,
-                     a->dtype == SAGA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                     const_cast<void*>(a->k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) {
-      *err = "cuTensorMapEncodeTiled failed for the key cache (" + std::to_string((int)r) + ")";
-      return SAGA_ERR_INVALID;
+    // the map depends only on the cache's address, dtype, extents and strides:
+    // the last few are kept (a decode loop cycles over one cache per layer)
+    const std::array<unsigned long long, 9> tkey = {(unsigned long long)reinterpret_cast<uintptr_t>(a->k),
+                                                    (unsigned long long)a->dtype, dims[0], dims[1], dims[2], dims[3],
+                                                    sl, sh, sb};
+    static std::mutex tmu;
+    static std::map<std::array<unsigned long long, 9>, CUtensorMap> tmaps;
+    bool have = false;
+    {
+      std::lock_guard<std::mutex> lock(tmu);
+      auto it = tmaps.find(tkey);
+      if (it != tmaps.end()) {
+        p.tmap = it->second;
+        have = true;
+      }
+    }
+    if (!have) {
+      CUresult r = enc(&p.tmap,
+                       a->dtype == SAGA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                       const_cast<void*>(a->k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        *err = "cuTensorMapEncodeTiled failed for the key cache (" + std::to_string((int)r) + ")";
+        return SAGA_ERR_INVALID;
+      }
+      std::lock_guard<std::mutex> lock(tmu);
+      if (tmaps.size() >= 256) tmaps.clear();
+      tmaps[tkey] = p.tmap;
     }
   }
 
