@@ -16,9 +16,9 @@
 
 namespace saga {
 
-const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask, bool shard);
-const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask, bool shard);
-const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask, bool shard);
+const void* pick_decode_kernel_bf16(int D, int mode, bool tc, bool mask, bool shard, bool paged);
+const void* pick_decode_kernel_fp16(int D, int mode, bool tc, bool mask, bool shard, bool paged);
+const void* pick_decode_kernel_fp32(int D, int mode, bool tc, bool mask, bool shard, bool paged);
 
 namespace {
 
@@ -44,10 +44,10 @@ DevInfo dev_info() {
 
 int esize_of(int dt) { return dt == SAGA_FP32 ? 4 : 2; }
 
-const void* pick_kernel(int dt, int D, int mode, bool tc, bool mask, bool shard) {
-  if (dt == SAGA_BF16) return pick_decode_kernel_bf16(D, mode, tc, mask, shard);
-  if (dt == SAGA_FP16) return pick_decode_kernel_fp16(D, mode, tc, mask, shard);
-  return pick_decode_kernel_fp32(D, mode, false, mask, shard);
+const void* pick_kernel(int dt, int D, int mode, bool tc, bool mask, bool shard, bool paged) {
+  if (dt == SAGA_BF16) return pick_decode_kernel_bf16(D, mode, tc, mask, shard, paged);
+  if (dt == SAGA_FP16) return pick_decode_kernel_fp16(D, mode, tc, mask, shard, paged);
+  return pick_decode_kernel_fp32(D, mode, false, mask, shard, paged);
 }
 
 const char* mode_name(int mode) {
@@ -115,10 +115,10 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
 int make_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, std::string* err) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const std::array<long long, 12> key = {dev, mode, a->dtype, a->B, a->Hq, a->Hk, a->Hv, a->D, a->L, a->nsel,
-                                         a->shards, a->mask != nullptr};
+  const std::array<long long, 13> key = {dev, mode, a->dtype, a->B, a->Hq, a->Hk, a->Hv, a->D, a->L, a->nsel,
+                                         a->shards, a->mask != nullptr, a->page_table != nullptr};
   static std::mutex mu;
-  static std::map<std::array<long long, 12>, DecodePlan> plans;
+  static std::map<std::array<long long, 13>, DecodePlan> plans;
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = plans.find(key);
@@ -213,9 +213,9 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
     const int want = 16 * ngg * std::max(1, std::min(4, 256 / (16 * ngg)));
     while (pl->tmem_cols < want) pl->tmem_cols *= 2;  // ngg <= 16 on this path: at most 256
   }
-  const void* kfn = pick_kernel(a->dtype, a->D, mode, tc, a->mask != nullptr, shards > 1);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, tc, a->mask != nullptr, shards > 1, a->page_table != nullptr);
   if (!kfn) {
-    *err = "no kernel for this combination of dtype, head_dim, op and sharding";
+    *err = "no kernel for this combination of dtype, head_dim, op, sharding and paging";
     return SAGA_ERR_UNSUPPORTED;
   }
   // The CTAs on one SM must fit its 512 TMEM columns together (an allocation
@@ -375,7 +375,7 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     }
   }
 
-  const void* kfn = pick_kernel(a->dtype, a->D, mode, pl.tc, a->mask != nullptr, shards > 1);
+  const void* kfn = pick_kernel(a->dtype, a->D, mode, pl.tc, a->mask != nullptr, shards > 1, a->page_table != nullptr);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(pl.grid);
   cfg.blockDim = dim3(kThreads);

@@ -105,10 +105,11 @@ __device__ __forceinline__ int page_of(const DecodeParams& p, int b, int pos) {
 // Element offset of the row of (sequence b, head h, position pos) in a cache
 // with strides (sb, sh, sl): contiguous, or inside page pg of a pool, sb then
 // being the page stride.
+template <bool PG>
 __device__ __forceinline__ int64_t cache_row(const DecodeParams& p, int64_t sb, int64_t sh, int64_t sl, int b, int h,
                                              int pos, int pg) {
-  return p.page_table ? (int64_t)pg * sb + (int64_t)h * sh + (int64_t)(pos & (p.page_len - 1)) * sl
-                      : (int64_t)b * sb + (int64_t)h * sh + (int64_t)pos * sl;
+  if constexpr (PG) return (int64_t)pg * sb + (int64_t)h * sh + (int64_t)(pos & (p.page_len - 1)) * sl;
+  else return (int64_t)b * sb + (int64_t)h * sh + (int64_t)pos * sl;
 }
 // Page of every 128-row tile of the item's chunk (paged caches), filled at
 // item start; it sits in the same shared-memory carve as misc.
@@ -119,21 +120,23 @@ __device__ __forceinline__ int* tile_pages(const DecodeParams& p, const Misc* mi
 // b: {y, b} for a contiguous cache; {row in page, page} for a paged one,
 // own tile t >= 0 from the chunk's tile pages, a tail tile (t < 0) from the
 // page table.
+template <bool PG>
 __device__ __forceinline__ void k_tile_coords(const DecodeParams& p, const Misc* misc, int b, int y, int t, int* ty,
                                               int* tw) {
-  if (!p.page_table) {
+  if constexpr (!PG) {
     *ty = y;
     *tw = b;
-    return;
+  } else {
+    *tw = t >= 0 ? tile_pages(p, misc)[t] : page_of(p, b, y);
+    *ty = y & (p.page_len - 1);
   }
-  *tw = t >= 0 ? tile_pages(p, misc)[t] : page_of(p, b, y);
-  *ty = y & (p.page_len - 1);
 }
 // Element offset of the value row of head vh at chunk position r (chunks
 // start on a tile boundary, so a tile lies in one page).
+template <bool PG>
 __device__ __forceinline__ int64_t value_row(const DecodeParams& p, const Misc* misc, int b, int vh, int p0, int r) {
-  return p.page_table ? cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, tile_pages(p, misc)[r >> 7])
-                      : cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, 0);
+  if constexpr (PG) return cache_row<true>(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, tile_pages(p, misc)[r >> 7]);
+  else return cache_row<false>(p, p.v_sb, p.v_sh, p.v_sl, b, vh, p0 + r, 0);
 }
 
 template <int MODE>
@@ -360,7 +363,7 @@ __device__ __forceinline__ float exp_term(float l, float m) {
 // Positions [a, a + cnt) are scored; with max_only they only raise
 // misc->tkey (the tail max), else they are stored at sc[(pos - p0) * SH + hl].
 // ---------------------------------------------------------------------------
-template <typename T, int D, bool MASK>
+template <typename T, int D, bool MASK, bool PG>
 __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, int cnt, int p0, bool max_only,
                                  const float* __restrict__ qf, T* __restrict__ sc, uint8_t* __restrict__ stage,
                                  Misc* misc) {
@@ -379,10 +382,12 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
       const int r = c / CPR, cc = c % CPR;
       const bool ok = (s * SUB + r) < cnt;
       const int pos = ok ? (a + s * SUB + r) : a;
-      const T* src = p.page_table ? reinterpret_cast<const T*>(p.k) +
-                                        cache_row(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, page_of(p, b, pos)) +
-                                        cc * (16 / (int)sizeof(T))
-                                  : kbase + (int64_t)pos * p.k_sl + cc * (16 / (int)sizeof(T));
+      const T* src;
+      if constexpr (PG)
+        src = reinterpret_cast<const T*>(p.k) + cache_row<true>(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, page_of(p, b, pos)) +
+              cc * (16 / (int)sizeof(T));
+      else
+        src = kbase + (int64_t)pos * p.k_sl + cc * (16 / (int)sizeof(T));
       cp_async16(buf + r * PITCH + cc * 16, src, ok);
     }
     cp_async_commit();
@@ -456,7 +461,7 @@ __device__ void score_range_simt(const DecodeParams& p, int b, int kh, int a, in
 // zero padded beyond G) is written into SMEM in the same 128-B swizzled
 // K-major layout the TMA produces for the key tiles.
 // ---------------------------------------------------------------------------
-template <typename T, int D, int MODE, bool MASK>
+template <typename T, int D, int MODE, bool MASK, bool PG>
 __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int n, int pre0, int n_pre,
                                T* __restrict__ sc, T* __restrict__ tsc, uint8_t* __restrict__ qop,
                                uint8_t* __restrict__ ring, Misc* misc, Ring& rg, uint32_t tmem_base) {
@@ -484,7 +489,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       }
       const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
       int ty, tw;
-      k_tile_coords(p, misc, b, y, q - n_pre, &ty, &tw);
+      k_tile_coords<PG>(p, misc, b, y, q - n_pre, &ty, &tw);
       mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
       uint8_t* dst = ring + rg.ps * TILE_BYTES;
 #pragma unroll
@@ -526,7 +531,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         }
         const int y = (q < n_pre) ? (pre0 + q) * 128 : p0 + (q - n_pre) * 128;
         int ty, tw;
-        k_tile_coords(p, misc, b, y, q - n_pre, &ty, &tw);
+        k_tile_coords<PG>(p, misc, b, y, q - n_pre, &ty, &tw);
         mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
         uint8_t* dst = ring + rg.ps * TILE_BYTES;
 #pragma unroll
@@ -947,7 +952,7 @@ __device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p,
 //     per warp, fixed-order reduction across warps, partial (m, l, o[D]) of
 //     every head published through the group's tagged slots.
 // ---------------------------------------------------------------------------
-template <typename T, int D>
+template <typename T, int D, bool PG>
 __device__ __forceinline__ void issue_rows(const DecodeParams& p, int b, int p0, const uint32_t* list, int e0,
                                            int rows, uint8_t* work, const Misc* misc) {
   constexpr int ROWB = D * (int)sizeof(T);
@@ -957,7 +962,7 @@ __device__ __forceinline__ void issue_rows(const DecodeParams& p, int b, int p0,
     const uint32_t ent = list[e0 + r];
     const int vh = misc->gvh[ent >> 24];
     const uint8_t* src = reinterpret_cast<const uint8_t*>(reinterpret_cast<const T*>(p.v) +
-                                                          value_row(p, misc, b, vh, p0, (int)(ent & 0xFFFFu)));
+                                                          value_row<PG>(p, misc, b, vh, p0, (int)(ent & 0xFFFFu)));
     cp_async16(work + (size_t)r * ROWB + c * 16, src + c * 16, true);
   }
   cp_async_commit();
@@ -986,7 +991,7 @@ __device__ __forceinline__ int pv_group_of(const Misc* misc, int ngroups, int s)
 // Copies of the value rows of global row slots [s0, s1) into pass slots
 // s - pbase: rows of real entries from the cache, padding slots zero-filled.
 // RPI = 2 rows per warp instruction, 16 segments each.
-template <typename T>
+template <typename T, bool PG>
 __device__ __noinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0, const uint32_t* __restrict__ list,
                                               uint8_t* __restrict__ work, const Misc* misc, int ngroups, int s0,
                                               int s1, int pbase) {
@@ -998,14 +1003,14 @@ __device__ __noinline__ void pv_issue_rows(const DecodeParams& p, int b, int p0,
     if (a >= z) continue;
     const int e0 = misc->gstart[gi], rows = misc->gstart[gi + 1] - e0, gbase = misc->gpad[gi];
     const T* vg = vb + (int64_t)misc->gvh[gi] * p.v_sh;
-    if (p.page_table) {  // paged: each row's page from the chunk's tile pages
+    if constexpr (PG) {  // paged: each row's page from the chunk's tile pages
       const T* v0 = reinterpret_cast<const T*>(p.v);
       for (int s = a + warp * 2 + sub; s < z; s += kWarps * 2) {
         const int r = s - gbase;
         uint8_t* dst = work + pv_row_off(s - pbase, sg);
         if (r < rows) {
           const int pos = (int)(list[e0 + r] & 0xFFFFu);
-          cp_async16(dst, v0 + value_row(p, misc, b, misc->gvh[gi], p0, pos) + sg * 8, true);
+          cp_async16(dst, v0 + value_row<true>(p, misc, b, misc->gvh[gi], p0, pos) + sg * 8, true);
         } else {
           cp_async16(dst, v0, false);
         }
@@ -1239,7 +1244,7 @@ __device__ __forceinline__ uint32_t task_occupancy(const uint32_t* __restrict__ 
 // TCPV: the kernel runs the tensor-core P.V (16-bit types at head_dim 128 on
 // the tensor-core scorer); otherwise the CUDA-core P.V's rows are issued here
 // when they fit one batch.
-template <typename T, int D, int MODE, bool TCPV>
+template <typename T, int D, int MODE, bool TCPV, bool PG>
 __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const T* __restrict__ sc,
                              const uint32_t* __restrict__ hmask, uint32_t* __restrict__ list, int* __restrict__ toff,
                              uint32_t* __restrict__ occ, uint8_t* __restrict__ work, uint8_t* __restrict__ wpv,
@@ -1320,7 +1325,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
   }
   if constexpr (TCPV) {
     if (p.sm.brw > 0) {  // tensor-core P.V: the first pass's rows
-      pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), 0);
+      pv_issue_rows<T, PG>(p, b, p0, list, work, misc, ngroups, 0, min(misc->gpad[ngroups], p.sm.brw), 0);
       cp_async_commit();
       trace_sub(p, 6);
     }
@@ -1334,9 +1339,11 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
 #pragma unroll 2
     for (int e = warp * RPI + sub; e < carry; e += kWarps * RPI) {
       const uint32_t ent = list[e];
-      const T* src = p.page_table ? reinterpret_cast<const T*>(p.v) +
-                                        value_row(p, misc, b, misc->gvh[ent >> 24], p0, (int)(ent & 0xFFFFu))
-                                  : vb + (int64_t)misc->gvh[ent >> 24] * p.v_sh + (int64_t)(ent & 0xFFFFu) * p.v_sl;
+      const T* src;
+      if constexpr (PG)
+        src = reinterpret_cast<const T*>(p.v) + value_row<true>(p, misc, b, misc->gvh[ent >> 24], p0, (int)(ent & 0xFFFFu));
+      else
+        src = vb + (int64_t)misc->gvh[ent >> 24] * p.v_sh + (int64_t)(ent & 0xFFFFu) * p.v_sl;
       cp_async16(work + (size_t)e * ROWB + seg * 16, reinterpret_cast<const uint8_t*>(src) + seg * 16, true);
     }
   }
@@ -1349,7 +1356,7 @@ __device__ void gather_begin(const DecodeParams& p, int b, int p0, int n, const 
 // accumulates out^T[d][head slot] += V^T[d][slot] * W[slot][head slot] into 16
 // TMEM columns per gather group. The partial (m, l, o[D]) of every head is
 // then published through the group's tagged slots.
-template <typename T, int D, int MODE, bool SHD>
+template <typename T, int D, int MODE, bool SHD, bool PG>
 __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0, const T* __restrict__ sc,
                               const uint32_t* __restrict__ hmask, const uint32_t* __restrict__ list,
                               uint8_t* __restrict__ work, uint8_t* __restrict__ wpv, Misc* misc, uint32_t tmem_base,
@@ -1373,7 +1380,7 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
   for (int ps0 = 0; ps0 < TS; ps0 += brw) {
     const int pn = min(brw, TS - ps0);
     if (ps0 > 0) {
-      pv_issue_rows<T>(p, b, p0, list, work, misc, ngroups, ps0, ps0 + pn, ps0);
+      pv_issue_rows<T, PG>(p, b, p0, list, work, misc, ngroups, ps0, ps0 + pn, ps0);
       cp_async_commit();
     }
     if (!(ps0 == 0 && w0_ready)) pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, ngroups, ps0, pn, false);
@@ -1467,7 +1474,7 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
   if (tr) trace_stamp(p, 14);
 }
 
-template <typename T, int D, int MODE, bool SHD>
+template <typename T, int D, int MODE, bool SHD, bool PG>
 __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, int p0, int n,
                            const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
                            const uint32_t* __restrict__ list, uint8_t* __restrict__ work, float* __restrict__ wbuf,
@@ -1519,7 +1526,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
       const int rows = min(BR, g1 - e0);
       int rbase = e0;  // SMEM row of entry e0
       if (!one_batch) {
-        issue_rows<T, D>(p, b, p0, list, e0, rows, work, misc);
+        issue_rows<T, D, PG>(p, b, p0, list, e0, rows, work, misc);
         weights(e0, rows);
         cp_async_wait<0>();
         __syncthreads();
@@ -1729,7 +1736,7 @@ __device__ __forceinline__ int find_bin(const int* hist256, int want, int* above
 // ---------------------------------------------------------------------------
 // The fused kernel.
 // ---------------------------------------------------------------------------
-template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD>
+template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD, bool PG>
 __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-aligned base (the 128-B swizzle pattern is taken from address bits)
@@ -1803,7 +1810,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 
     // ---- paged caches: the page of each of the chunk's tiles (read by the
     // scorer's TMA and by the value-row gathers after the next barrier)
-    if (p.page_table) {
+    if constexpr (PG) {
       int* tpg = tile_pages(p, misc);
       for (int t = threadIdx.x; t < (n + 127) / 128; t += kThreads) tpg[t] = page_of(p, b, p0 + t * 128);
     }
@@ -1821,15 +1828,16 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     if (p.k_new && apos >= 0) {
       const int pos = apos;
       const T* src = reinterpret_cast<const T*>(p.k_new) + (int64_t)b * p.kn_sb + (int64_t)kh * p.kn_sh;
-      const int apg = p.page_table ? page_of(p, b, pos) : 0;  // an append goes to a page of its own sequence
-      T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + cache_row(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, apg);
+      int apg = 0;  // an append goes to a page of its own sequence
+      if constexpr (PG) apg = page_of(p, b, pos);
+      T* dst = const_cast<T*>(reinterpret_cast<const T*>(p.k)) + cache_row<PG>(p, p.k_sb, p.k_sh, p.k_sl, b, kh, pos, apg);
       for (int d = threadIdx.x; d < D; d += kThreads) dst[d] = src[d];
       if (p.v_new && pos >= p0 && pos < p0 + n) {
         const int vh_lo = h0 / p.Gv, vh_hi = (h0 + G - 1) / p.Gv;
         for (int i = threadIdx.x; i < (vh_hi - vh_lo + 1) * D; i += kThreads) {
           const int vh = vh_lo + i / D, d = i % D;
           const T* vs = reinterpret_cast<const T*>(p.v_new) + (int64_t)b * p.vn_sb + (int64_t)vh * p.vn_sh;
-          T* vd = const_cast<T*>(reinterpret_cast<const T*>(p.v)) + cache_row(p, p.v_sb, p.v_sh, p.v_sl, b, vh, pos, apg);
+          T* vd = const_cast<T*>(reinterpret_cast<const T*>(p.v)) + cache_row<PG>(p, p.v_sb, p.v_sh, p.v_sl, b, vh, pos, apg);
           vd[d] = vs[d];
         }
       }
@@ -1846,7 +1854,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         n_pre = (p.L + kTile - 1) / kTile - pre0;
       }
       __syncthreads();
-      score_chunk_tc<T, D, MODE, MASK>(p, b, kh, p0, n, pre0, n_pre, sc, tsc, qop, work, misc, rg, tmem_base);
+      score_chunk_tc<T, D, MODE, MASK, PG>(p, b, kh, p0, n, pre0, n_pre, sc, tsc, qop, work, misc, rg, tmem_base);
       const int ej2 = (MODE == MODE_AMORTIZED) ? 2 * epilogue_exp_pairs(G) : 0;
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         if (hl < ej2) {  // heads folded by the epilogue warps
@@ -1867,8 +1875,8 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       for (int hl = threadIdx.x; hl < kMaxG; hl += kThreads) misc->tkey[hl] = 0u;
       __syncthreads();
       if (MODE == MODE_AMORTIZED)
-        score_range_simt<T, D, MASK>(p, b, kh, tail_start, p.tail, p0, true, qf, sc, work, misc);
-      score_range_simt<T, D, MASK>(p, b, kh, p0, n, p0, false, qf, sc, work, misc);
+        score_range_simt<T, D, MASK, PG>(p, b, kh, tail_start, p.tail, p0, true, qf, sc, work, misc);
+      score_range_simt<T, D, MASK, PG>(p, b, kh, p0, n, p0, false, qf, sc, work, misc);
       for (int hl = warp; hl < G; hl += kWarps) {
         const float m = funkey(misc->tkey[hl]);
         float s = 0.f, mx = -INFINITY;
@@ -1952,7 +1960,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       }
       // lists, value-row copies and the first pass's weights go out while the
       // counts are exchanged
-      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       SAGA_TRACE(3)
       slots_gather_field<SHD>(p, g, kSlotCnt, tag, xbuf);
       __syncthreads();
@@ -2047,10 +2055,10 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         // heads capped at K changed their bits and stabiliser: redo their weights
         pv_weights<T, MODE>(p, sc, hmask, list, wpv, misc, misc->ngroups, 0,
                             min(misc->gpad[misc->ngroups], p.sm.brw), true);
-        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, true);
+        gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, true);
       }
       else
-        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else if constexpr (MODE == MODE_CALIBRATE) {
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
@@ -2177,17 +2185,17 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         hmask[i] = bits;
       }
       __syncthreads();
-      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
-        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+        gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else
-        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
-      gather_begin<T, D, MODE, kTcPv>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+      gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
-        gather_end_tc<T, D, MODE, SHD>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+        gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
       else
-        gather_end<T, D, MODE, SHD>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+        gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     }
     __syncthreads();
 
@@ -2264,14 +2272,16 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
 }
 
 
-// Kernel entry of one (dtype, head_dim, mode, scorer, mask, sharded) combination.
-template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD>
+// Kernel entry of one (dtype, head_dim, mode, scorer, mask, sharded, paged) combination.
+template <typename T, int D, int MODE, bool TC, bool MASK, bool SHD, bool PG = false>
 const void* decode_kernel_ptr() {
-  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE, TC, MASK, SHD>);
+  return reinterpret_cast<const void*>(&saga_decode_kernel<T, D, MODE, TC, MASK, SHD, PG>);
 }
 
-// Sharded kernels exist for the decode and dense modes on the tensor-core path.
-template <typename T, bool TC, bool MASK, bool SHD>
+// Sharded kernels exist for the decode and dense modes on the tensor-core
+// path; paged ones (PG) for every mode, not sharded. Paging is a separate
+// instantiation so that the contiguous kernels carry none of its code.
+template <typename T, bool TC, bool MASK, bool SHD, bool PG = false>
 const void* pick_d_mode(int D, int mode) {
   if constexpr (SHD) {
     if (!TC) return nullptr;
@@ -2286,17 +2296,17 @@ const void* pick_d_mode(int D, int mode) {
   } else {
     if (D == 64) {
       switch (mode) {
-        case MODE_AMORTIZED: return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK, false>();
-        case MODE_CALIBRATE: return decode_kernel_ptr<T, 64, MODE_CALIBRATE, TC, MASK, false>();
-        case MODE_DENSE: return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK, false>();
-        default: return decode_kernel_ptr<T, 64, MODE_LOGITS, TC, MASK, false>();
+        case MODE_AMORTIZED: return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK, false, PG>();
+        case MODE_CALIBRATE: return decode_kernel_ptr<T, 64, MODE_CALIBRATE, TC, MASK, false, PG>();
+        case MODE_DENSE: return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK, false, PG>();
+        default: return decode_kernel_ptr<T, 64, MODE_LOGITS, TC, MASK, false, PG>();
       }
     }
     switch (mode) {
-      case MODE_AMORTIZED: return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK, false>();
-      case MODE_CALIBRATE: return decode_kernel_ptr<T, 128, MODE_CALIBRATE, TC, MASK, false>();
-      case MODE_DENSE: return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK, false>();
-      default: return decode_kernel_ptr<T, 128, MODE_LOGITS, TC, MASK, false>();
+      case MODE_AMORTIZED: return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK, false, PG>();
+      case MODE_CALIBRATE: return decode_kernel_ptr<T, 128, MODE_CALIBRATE, TC, MASK, false, PG>();
+      case MODE_DENSE: return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK, false, PG>();
+      default: return decode_kernel_ptr<T, 128, MODE_LOGITS, TC, MASK, false, PG>();
     }
   }
 }
