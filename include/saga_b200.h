@@ -104,7 +104,9 @@ typedef struct SagaAttnArgs {
    * after the exchanges and gather steps), column 64 + k = global timer (ns)
    * at the same point; 16 + t / 32 + t / 48 + t = SM clock when key tile t
    * (< 16) was issued by TMA / multiplied / stored; 127 = value rows
-   * gathered. Diagnostics only. */
+   * gathered. Diagnostics only: written only by a library built with
+   * SAGA_PHASE_TRACE=1 in the environment (python -m saga_b200.build --force),
+   * ignored otherwise. */
   int64_t* trace;
 
   /* Sequence sharding (config 4 of the reference's benchmarks): the positions

@@ -24,6 +24,10 @@ STAMP = os.path.join(HERE, ".libsaga_b200.stamp")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
          "-Xcompiler", "-fvisibility=hidden", "-Xptxas", "-v"]
+# SAGA_PHASE_TRACE=1 in the environment builds the diagnostic phase trace in
+# (SagaAttnArgs.trace); the default build leaves it out of the kernels.
+if os.environ.get("SAGA_PHASE_TRACE") == "1":
+    FLAGS.append("-DSAGA_PHASE_TRACE=1")
 
 
 def _nvcc() -> str:

@@ -155,14 +155,20 @@ struct Ring {
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
 };
 
-// Optional phase trace (diagnostics). The stores are out of line, so that a
-// stamp site costs one test of p.trace when tracing is off.
+// Optional phase trace (diagnostics), compiled in only when the library is
+// built with SAGA_PHASE_TRACE=1: otherwise every stamp site compiles to
+// nothing and SagaAttnArgs.trace is ignored (the stamp sites are many, and
+// code size costs the latency-bound phases instruction fetches).
 //  * trace_stamp(k), k < 16: SM clock at column k, global timer (ns,
 //    comparable across SMs) at column 64 + k;
 //  * trace_sub(k), k < 40: SM clock at column 80 + k, written by thread 0 of
 //    CTA c < 1024 (its last item wins): where a phase spends its time;
 //  * trace_col(col, v): raw value (columns 16-63 tile stamps, 120-122 global
 //    timer at kernel entry, after set-up and at exit, 127 rows gathered).
+#ifndef SAGA_PHASE_TRACE
+#define SAGA_PHASE_TRACE 0
+#endif
+constexpr bool kTrace = SAGA_PHASE_TRACE != 0;
 static __device__ __noinline__ void trace_write(long long* trace, int col, long long v) {
   trace[blockIdx.x * kTraceCols + col] = v;
 }
@@ -171,13 +177,16 @@ static __device__ __noinline__ void trace_stamp_now(long long* trace, int k) {
   trace[blockIdx.x * kTraceCols + 64 + k] = (long long)globaltimer_ns();
 }
 __device__ __forceinline__ void trace_stamp(const DecodeParams& p, int k) {
-  if (p.trace && blockIdx.x < 1024) trace_stamp_now(p.trace, k);
+  if constexpr (kTrace)
+    if (p.trace && blockIdx.x < 1024) trace_stamp_now(p.trace, k);
 }
 __device__ __forceinline__ void trace_sub(const DecodeParams& p, int k) {
-  if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) trace_write(p.trace, 80 + k, clock64());
+  if constexpr (kTrace)
+    if (p.trace && threadIdx.x == 0 && blockIdx.x < 1024) trace_write(p.trace, 80 + k, clock64());
 }
 __device__ __forceinline__ void trace_col(const DecodeParams& p, int col, long long v) {
-  if (p.trace && blockIdx.x < 1024) trace_write(p.trace, col, v);
+  if constexpr (kTrace)
+    if (p.trace && blockIdx.x < 1024) trace_write(p.trace, col, v);
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -1370,7 +1379,7 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
   const int TS = misc->gpad[ngroups];
   // accumulators per gather group: as many as the TMEM columns allow, at most 4
   const int nch = min(4, p.tmem_cols / (16 * max(ngroups, 1)));
-  const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
+  const bool tr = kTrace && p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
   if (tr) trace_col(p, 127, misc->gstart[ngroups]);
   for (int t = threadIdx.x; t < ngroups * 8; t += kThreads) misc->lacc[t] = 0.f;
   if (brw < 16) {  // unreachable by construction of the layout; no pass could run
@@ -1502,7 +1511,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
       wbuf[i] = wv;
     }
   };
-  const bool tr = p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
+  const bool tr = kTrace && p.trace && threadIdx.x == 0 && blockIdx.x < 1024;
   if (tr) trace_col(p, 127, total);
   if (one_batch && total > 0) {
     weights(0, total);
@@ -1800,7 +1809,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G] (calibration)
     ChunkStat* st = stg + (size_t)j * G;
     const int row0 = b * p.Hq + h0;
-    const bool tracing = p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
+    const bool tracing = kTrace && p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
 #define SAGA_TRACE(k) \
   if (tracing) trace_stamp(p, (k));
     SAGA_TRACE(0)
