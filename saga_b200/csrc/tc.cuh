@@ -60,9 +60,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 // Wait for the phase of `parity` to complete, at most kWaitLimitNs. Returns
 // false (and flags the status word) on timeout. The first try waits in
-// hardware (up to ~1 ms); the bounded retry loop is out of line, so that the
-// many wait sites stay small.
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* status) {
+// hardware (up to ~1 ms); then a bounded retry loop. The loop is inlined: as
+// an out-of-line call it cost more code at each wait site (the call's
+// register saves) and constrained the per-tile loops around it.
+__device__ __forceinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* status) {
   const unsigned long long t0 = globaltimer_ns();
   while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
