@@ -2,7 +2,7 @@
 
 The fixtures come from running noamelata/SAGA's ``attention/attention.py`` and
 ``attention/triton_atopn.py`` on CPU (``tests/golden/make_golden.py``). These
-tests pin the oracle before it is used to judge the CUDA path.
+tests pin the oracle before it is used to check the CUDA path.
 """
 import numpy as np
 import pytest
