@@ -182,11 +182,15 @@ SAGA_API int saga_atopn_decode(const SagaAttnArgs* args, void* stream);
  * reference: it serves hosts that cannot allocate device memory at call time.
  * The scratch is a fixed array of saga_noalloc_scratch_bytes() (8 MiB) in the
  * library's own device memory, one per device; shapes that need more are
- * refused with SAGA_ERR_WORKSPACE (args->workspace is ignored). Each call
- * zero-fills the bytes it uses with one cudaMemsetAsync on `stream`. Calls on
- * one device must not overlap on the GPU: they share the scratch. Make the
- * first call on a device outside stream capture (it looks the array's address
- * up once). Nothing is allocated. */
+ * refused with SAGA_ERR_WORKSPACE (args->workspace is ignored). The array is
+ * part of the library's device image, so every CUDA context that loads the
+ * library holds those 8 MiB until exit, whether or not this entry point is
+ * called. Sequence sharding (shards > 1) is refused with SAGA_ERR_UNSUPPORTED.
+ * A call is fully validated before it touches the scratch; then it zero-fills
+ * the bytes it uses with one cudaMemsetAsync on `stream`. Calls on one device
+ * must not overlap on the GPU: they share the scratch. Make the first call on
+ * a device outside stream capture (it may load the library's device code
+ * there). Nothing is allocated. */
 SAGA_API int saga_atopn_decode_noalloc(const SagaAttnArgs* args, void* stream);
 
 /* Capacity in bytes of the static scratch of saga_atopn_decode_noalloc. */

@@ -131,6 +131,12 @@ int run_attn(const SagaAttnArgs* a, int op, void* stream) {
 namespace saga {
 // Error reporting for entry points defined in other files.
 int abi_fail(int code, const std::string& msg) { return fail(code, msg); }
+// The full host-side validation of an attention call (no launch).
+int abi_check(const SagaAttnArgs* a, int op) {
+  int rc = check_shapes(a);
+  if (rc || a->B == 0) return rc;
+  return check_attn(a, op);
+}
 }  // namespace saga
 
 extern "C" {

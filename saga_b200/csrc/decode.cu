@@ -205,9 +205,9 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
   pl->nvh = ngg;
   pl->tc = tc;
   pl->cooperative = (mode != MODE_LOGITS);
-  // TMEM columns per CTA: the scorer's two 16-column accumulators, or output
-  // and weight sums (2 x 16 columns) per gather group for the tensor-core P.V
-  pl->tmem_cols = 32;
+  // TMEM columns per CTA: the scorer's kScoreBufs 16-column accumulators, or
+  // up to 4 x 16 columns per gather group for the tensor-core P.V
+  pl->tmem_cols = 16 * kScoreBufs;
   if (uses_tc_pv(tc, a->D)) {
     // up to 4 16-column accumulators per gather group, within 256 columns
     const int want = 16 * ngg * std::max(1, std::min(4, 256 / (16 * ngg)));

@@ -29,6 +29,7 @@ constexpr int kCtrlDone = 31;   // index of the group's completion counter (this
 constexpr int kCtrlShardsDone = 30;  // sharded, on shard 0: devices whose chunks are all done
 constexpr int kMaxG = 32;       // query heads per key head supported
 constexpr int kMaxStages = 4;   // K-tile ring depth of the tensor-core scorer
+constexpr int kScoreBufs = 2;   // TMEM accumulators of the tensor-core scorer (16 columns each)
 constexpr int kMaxGatherGroups = 64;
 constexpr int kMaxShards = 8;   // devices a sequence can be sharded over
 
@@ -106,7 +107,7 @@ struct DecodeParams {
   CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
   int B, Hq, Hk, Hv, D, L, G, Gv;
   int C, CL, items, tail, buf_k, ns, nvh, sh;
-  int tmem_cols;  // TMEM columns per CTA: the scorer's 2 x 16, or up to 4 x 16 per gather group for the P.V
+  int tmem_cols;  // TMEM columns per CTA: the scorer's kScoreBufs x 16, or up to 4 x 16 per gather group for the P.V
   const void* q; int64_t q_sb, q_sh;
   const void* k; int64_t k_sb, k_sh, k_sl;
   const void* v; int64_t v_sb, v_sh, v_sl;

@@ -52,8 +52,8 @@ namespace saga {
 struct Misc {
   uint64_t full[kMaxStages];   // K tile landed (TMA complete_tx)
   uint64_t empty[kMaxStages];  // K stage free again (UMMA commit)
-  uint64_t tfull[2];           // TMEM accumulator ready (UMMA commit)
-  uint64_t tempty[2];          // TMEM accumulator drained (4 epilogue warps)
+  uint64_t tfull[kScoreBufs];  // TMEM accumulator ready (UMMA commit)
+  uint64_t tempty[kScoreBufs]; // TMEM accumulator drained (4 epilogue warps)
   uint32_t tmem_slot;
   int abort;
   uint32_t tag;                // exchange tag of this launch for the current group
@@ -264,15 +264,15 @@ __device__ __forceinline__ unsigned long long slot_ld(const unsigned long long* 
 // re-polls all of its pending slots together, so a late publisher costs one
 // round trip, not one per slot. Bounded: after kWaitLimitNs the status word
 // gets SAGA_STATUS_WAIT_TIMEOUT and the stale values are used.
-template <bool SHD, typename AddrFn>
+template <bool SHD, int NT = kThreads, typename AddrFn>
 __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t tag, uint32_t* dst, int* status) {
-  for (int base = threadIdx.x; base < count; base += kThreads * 8) {
+  for (int base = threadIdx.x; base < count; base += NT * 8) {
     const unsigned long long* a[8];
     unsigned long long v[8];
     uint32_t pending = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int i = base + k * kThreads;
+      const int i = base + k * NT;
       a[k] = (i < count) ? addr(i) : nullptr;
       if (i < count) pending |= 1u << k;
     }
@@ -284,7 +284,7 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         if (((pending >> k) & 1u) && (uint32_t)(v[k] >> 32) == tag) {
-          dst[base + k * kThreads] = (uint32_t)v[k];
+          dst[base + k * NT] = (uint32_t)v[k];
           pending &= ~(1u << k);
         }
       }
@@ -297,7 +297,7 @@ __device__ __forceinline__ void slots_gather(int count, AddrFn addr, uint32_t ta
           if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            if ((pending >> k) & 1u) dst[base + k * kThreads] = (uint32_t)v[k];
+            if ((pending >> k) & 1u) dst[base + k * NT] = (uint32_t)v[k];
           break;
         }
       }
@@ -316,13 +316,13 @@ __device__ __forceinline__ unsigned long long* shard_slot(const DecodeParams& p,
 // Exchange of one per-(chunk, head) scalar field of group g over this
 // device's chunks: dst[c * G + hl] for local chunk c (all of the group's
 // chunks when the sequence is not sharded). One out-of-line copy serves
-// every such exchange.
-template <bool SHD>
+// every such exchange. NT threads take part.
+template <bool SHD, int NT = kThreads>
 static __device__ __noinline__ void slots_gather_field(const DecodeParams& p, int g, int field, uint32_t tag,
                                                        uint32_t* dst) {
   const FastDiv divg((uint32_t)p.G);
   const int c0 = SHD ? p.shard * p.c_local : 0;
-  slots_gather<SHD>(
+  slots_gather<SHD, NT>(
       p.c_local * p.G,
       [&](int i) {
         const int c = (int)divg.div((uint32_t)i);
@@ -597,7 +597,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
           rg.ms = 0;
           rg.mph ^= 1u;
         }
-        if (++rg.mb == 2u) {
+        if (++rg.mb == (uint32_t)kScoreBufs) {
           rg.mb = 0;
           rg.mbph ^= 1u;
         }
@@ -636,7 +636,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&misc->tempty[rg.eb]);
-      if (++rg.eb == 2u) {
+      if (++rg.eb == (uint32_t)kScoreBufs) {
         rg.eb = 0;
         rg.ebph ^= 1u;
       }
@@ -1597,7 +1597,7 @@ __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, i
 // combination order is fixed. A record's partial outputs are [head][d], so
 // the slice of source k is one run of consecutive slots from
 // rec(k) + kSlotO * G + lo.
-template <int D, int MODE, bool SHD, typename Rec, typename Emit>
+template <int D, int MODE, bool SHD, int NT = kThreads, typename Rec, typename Emit>
 __device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, int nout, int hl0, int nhs, uint32_t tag,
                             uint8_t* scratch, Emit emit, Misc* misc, bool final_level) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -1606,7 +1606,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, in
   const int n_ml = nhs * nsrc * 2;
   const int G = p.G;
   const FastDiv div2c((uint32_t)(2 * nsrc)), divn((uint32_t)nout);
-  slots_gather<SHD>(
+  slots_gather<SHD, NT>(
       n_ml + nout * nsrc,
       [&](int i) {
         if (i < n_ml) {
@@ -1622,7 +1622,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, in
   __syncthreads();
   trace_sub(p, 26);
   float* scl = reinterpret_cast<float*>(ov + nout * nsrc);  // [nhs][nsrc]
-  for (int hh = warp; hh < nhs; hh += kWarps) {
+  for (int hh = warp; hh < nhs; hh += NT / 32) {
     float M = -INFINITY;
     for (int c = lane; c < nsrc; c += 32) M = nanmax(M, __uint_as_float(ml[(hh * nsrc + c) * 2]));
     M = warp_nanmax(M);
@@ -1643,7 +1643,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, in
     }
   }
   __syncthreads();
-  for (int k = threadIdx.x; k < nout; k += kThreads) {
+  for (int k = threadIdx.x; k < nout; k += NT) {
     const int hh = (lo + k) / D - hl0;
     float a = 0.f;
     for (int c = 0; c < nsrc; ++c) a += __uint_as_float(ov[c * nout + k]) * scl[hh * nsrc + c];
@@ -1657,7 +1657,7 @@ __device__ void merge_level(const DecodeParams& p, int nsrc, Rec rec, int lo, in
 // combined partial is published; then over the devices' partials of the same
 // slice (CTA jl of every device covers the same outputs). Every device writes
 // all outputs.
-template <typename T, int D, int MODE, bool SHD>
+template <typename T, int D, int MODE, bool SHD, int NT = kThreads>
 __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0, uint8_t* scratch, Misc* misc) {
   const int G = p.G;
   const int tot = G * D;
@@ -1676,7 +1676,7 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
     *out = Num<T>::from_f(a / misc->lsum[hh]);
   };
   if constexpr (!SHD) {
-    merge_level<D, MODE, false>(
+    merge_level<D, MODE, false, NT>(
         p, p.c_local, [&](int c) { return slot_at<false>(p, g, c, 0, 0); }, lo, nout, hl0, nhs, tag,
         scratch, write_out, misc, true);
     if (threadIdx.x == 0) trace_stamp(p, 15);
@@ -1778,7 +1778,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       mbar_init(&misc->full[s], 1);
       mbar_init(&misc->empty[s], 1);
     }
-    for (int bb = 0; bb < 2; ++bb) {
+    for (int bb = 0; bb < kScoreBufs; ++bb) {
       mbar_init(&misc->tfull[bb], 1);
       mbar_init(&misc->tempty[bb], 4);
     }

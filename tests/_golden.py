@@ -76,6 +76,53 @@ def near_threshold_ok(x_row: np.ndarray, t: float, diff_idx, dtype: str, n_ulps:
     return bool(np.all(np.abs(xs - np.float32(t)) <= tol))
 
 
+def calib_row_ok(probs_row: np.ndarray, pn: float, thr: float, ours, ref, dtype: str):
+    """One row of a calibration step against a checker that ran on the same
+    logits. ``probs_row`` and ``pn`` are the checker's probabilities and N-th
+    largest probability, ``thr`` the kernel's threshold; ``ours`` / ``ref`` are
+    the kept positions. Two exp / sum implementations can round a probability
+    one ulp apart, so the rule is the parity bar with no allowance beyond that:
+    the thresholds are equal or one ulp apart, and every position kept by one
+    side only has a probability within one ulp of pN (a tie at the threshold).
+    Returns (ok, reason)."""
+    pn = np.float32(pn)
+    thr = np.float32(thr)
+    if dtype == "fp32":
+        tol = np.float32(1e-5) * abs(pn) + ulp(pn, "fp32")
+    else:
+        tol = ulp(pn, dtype)
+    if abs(thr - pn) > tol:
+        return False, f"threshold {thr!r} vs {pn!r}: more than one ulp apart"
+    d = np.asarray(sorted(set(np.asarray(ours).tolist()) ^ set(np.asarray(ref).tolist())), dtype=np.int64)
+    if len(d):
+        off = np.abs(probs_row[d] - pn)
+        if not np.all(off <= tol):
+            bad = d[off > tol]
+            return False, f"positions {bad[:8].tolist()} kept by one side only are not ties at pN"
+    return True, ""
+
+
+def amortized_set_ok(lg_ref: np.ndarray, lg_ours: np.ndarray, t: float, ours, ref, dtype: str, fp32_tol: float):
+    """Selected sets of one amortized row. A position kept by one side only is
+    allowed when its reference logit lies within one ulp of the threshold t (a
+    tie), or when the kernel's own logit for it differs from the reference's
+    (the GEMM accumulation order, bounded by the logits test) by at least the
+    distance of the reference logit from t beyond that ulp. Nothing else may
+    differ."""
+    d = np.asarray(sorted(set(np.asarray(ours).tolist()) ^ set(np.asarray(ref).tolist())), dtype=np.int64)
+    if len(d) == 0:
+        return True
+    xr = lg_ref[d].astype(np.float32)
+    xo = lg_ours[d].astype(np.float32)
+    t = np.float32(t)
+    if dtype == "fp32":
+        tie = np.float32(fp32_tol)
+    else:
+        tie = np.maximum(ulp(xr, dtype), ulp(t, dtype))
+    dist = np.abs(xr - t)
+    return bool(np.all(dist <= tie + np.abs(xo - xr)))
+
+
 def rel_rms(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)

@@ -2,9 +2,14 @@
 vectors and the CPU oracle.
 
 Tolerances (from the parity target of this path):
-  * selected index sets: identical to the reference's, except positions whose
-    logit is within 1 ulp of the threshold (bf16/fp16). For fp32 the logits of
-    any two GEMM orders differ by ~1e-6, so the window is FP32_LOGIT_TOL;
+  * amortized selected sets: identical to the reference's, except positions
+    whose reference logit is within 1 ulp of the threshold (bf16/fp16), or
+    whose kernel logit deviates from the reference's (bounded by test_logits)
+    by at least that logit's distance from the threshold. For fp32 the logits
+    of any two GEMM orders differ by ~1e-6, so the window is FP32_LOGIT_TOL;
+  * calibration, every row: the threshold equals the checker's N-th largest
+    probability or lies one ulp from it, and the kept sets differ only at
+    positions whose probability is within that ulp of it (ties);
   * outputs: bf16/fp16 max-abs <= 2e-2 and relative RMS <= 1e-2; fp32 max-abs <= 1e-4;
   * logits: at most 2 ulps (GEMM accumulation order, then the second rounding
     after ``* scaling``), on < 0.1 % of elements.
@@ -14,7 +19,7 @@ import pytest
 import torch
 
 from oracle import atopn_oracle as O
-from _golden import load, golden_names, near_threshold_ok, rel_rms, ulp
+from _golden import load, golden_names, rel_rms, ulp, calib_row_ok, amortized_set_ok
 
 pytestmark = pytest.mark.gpu
 
@@ -43,14 +48,6 @@ def _out_ok(out, ref, dtype):
     if dtype == "fp32":
         return np.abs(out - ref).max() <= FP32_MAXABS
     return np.abs(out - ref).max() <= BF16_MAXABS and rel_rms(out, ref) <= BF16_RELRMS
-
-
-def _sets_ok(lg_row, t, ours, ref, dtype):
-    d = set(ours) ^ set(ref)
-    if dtype == "fp32":
-        xs = lg_row[np.asarray(sorted(d), dtype=np.int64)] if d else np.zeros(0)
-        return bool(np.all(np.abs(xs - t) <= FP32_LOGIT_TOL))
-    return near_threshold_ok(lg_row, t, d, dtype)
 
 
 @pytest.fixture(scope="module")
@@ -169,6 +166,10 @@ def test_atopn_decode_fused(gold, name, fused_append):
     t = _np(diag["logit_thr"])
     np.testing.assert_allclose(t, g["t1"], rtol=1e-5, atol=1e-6)
     lg = _np(ops.attn_logits(_t(inp.q1, dt), _t(k1, dt), _mask_t(g))).reshape(R, -1)
+    # the tie window is judged on the reference's own logits where the
+    # fixture stores them; the kernel's logits only explain a difference
+    # through their own (separately bounded) deviation from the reference's
+    lg_ref = g["logits1"] if g.has("logits1") else lg
     cnt = diag["count"].cpu().numpy()
     sel = diag["sel_idx"].cpu().numpy()
     kk = g.meta["buf_k"]
@@ -180,7 +181,8 @@ def test_atopn_decode_fused(gold, name, fused_append):
             assert kept == kk and np.all(lg[r, ours] > t[r])
             continue
         ref = g["sel_idx"][r, :g["sel_kept"][r]].astype(np.int64)
-        assert _sets_ok(lg[r], g["t1"][r], ours.tolist(), ref.tolist(), dt), (r, set(ours) ^ set(ref))
+        assert amortized_set_ok(lg_ref[r], lg[r], g["t1"][r], ours, ref, dt, FP32_LOGIT_TOL), \
+            (r, set(ours.tolist()) ^ set(ref.tolist()))
     if name == "overflow_bf16":
         res = O.atopn_amortized(inp.q1, k1, v1, g["thr_used"], g.shape.N, dt, mask=g.mask())
         assert _out_ok(_np(out).reshape(R, D), res["out"].reshape(R, D), dt)
@@ -199,21 +201,28 @@ def test_atopn_calibrate(gold, name):
     out = ops.atopn_calibrate(_t(inp.q0, dt), _t(inp.k, dt), _t(inp.v, dt), _mask_t(g), thr, g.shape.N,
                               None, diag=diag)
     thr = _np(thr)
-    # oracle on the kernel's own logits: identical threshold and set
+    n = min(g.shape.N, g.shape.L)
+    sel = diag["sel_idx"].cpu().numpy()
+    # (1) the oracle on the kernel's own logits: every row's threshold and kept
+    # set equal, except ties within one ulp of pN
     lg = _np(ops.attn_logits(_t(inp.q0, dt), _t(inp.k, dt), _mask_t(g))).reshape(R, -1)
     probs = O.softmax_dtype(lg, dt)
-    n = min(g.shape.N, g.shape.L)
     pn, idx, _ = O.topn_threshold(probs, n)
-    if dt == "fp32":
-        np.testing.assert_allclose(thr, pn, rtol=1e-5)
-        np.testing.assert_allclose(thr, g["thr"], rtol=1e-4)
-    else:
-        assert (thr == pn).mean() >= 0.99
-        assert (thr == g["thr"]).mean() >= 0.95
-    sel = diag["sel_idx"].cpu().numpy()
     for r in range(R):
-        if thr[r] == pn[r]:
-            np.testing.assert_array_equal(sel[r, :n], idx[r])
+        assert np.all(np.diff(sel[r, :n]) > 0)
+        ok, why = calib_row_ok(probs[r], pn[r], thr[r], sel[r, :n], idx[r], dt)
+        assert ok, (r, why)
+    # (2) the reference itself (its threshold and top-N positions), on every
+    # row whose logits the kernel reproduces bit for bit; the other rows differ
+    # only through logits that test_logits bounds, and (1) covers them
+    if g.has("logits0"):
+        lg_ref = g["logits0"]
+        probs_ref = O.softmax_dtype(lg_ref, dt)
+        same = np.all(lg == lg_ref, axis=-1) if dt != "fp32" else np.ones(R, bool)
+        for r in np.nonzero(same)[0]:
+            ok, why = calib_row_ok(probs_ref[r], g["thr"][r], thr[r], sel[r, :n],
+                                   g["ref_top_idx"][r].astype(np.int64), dt)
+            assert ok, (r, "vs reference", why)
     w = np.take_along_axis(probs, idx, axis=-1)
     ref_out = O.gather_output(w, idx, inp.v, g.shape.B, g.shape.Hq, dt, False).reshape(R, D)
     assert _out_ok(_np(out).reshape(R, D), ref_out, dt)

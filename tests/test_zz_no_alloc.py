@@ -100,3 +100,25 @@ def test_noalloc_rejects_shapes_beyond_the_scratch():
     rc = L.lib.saga_atopn_decode_noalloc(ctypes.byref(a), ctypes.c_void_p(ops._stream(q.device)))
     assert rc == L.SAGA_ERR_WORKSPACE
     assert "static scratch" in L.lib.saga_last_error().decode()
+
+
+def test_noalloc_refuses_sharding_and_bad_args_before_touching_the_scratch():
+    """A sharded call and an invalid call are refused up front; the scratch
+    (whose last contents a later call must not depend on) is left alone, so a
+    following valid call still matches the regular entry point."""
+    shape = SHAPES[0]
+    q, k, v = _inputs(shape, 11)
+    thr = _thresholds(shape, q, k, v)
+    out = torch.empty_like(q)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = _args(q, k, v, thr, shape[-1], out, status)
+    a.shards, a.shard = 2, 0
+    stream = ctypes.c_void_p(ops._stream(q.device))
+    assert L.lib.saga_atopn_decode_noalloc(ctypes.byref(a), stream) == L.SAGA_ERR_UNSUPPORTED
+    assert "sharding" in L.lib.saga_last_error().decode()
+    a.shards, a.shard = 0, 0
+    a.thr_in = None
+    assert L.lib.saga_atopn_decode_noalloc(ctypes.byref(a), stream) == L.SAGA_ERR_INVALID
+    ref, ref_st = _regular(shape, q, k, v, thr)
+    got, st = _noalloc(shape, q, k, v, thr)
+    assert st == ref_st and torch.equal(got, ref)
