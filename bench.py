@@ -17,9 +17,14 @@ transform, selection and the sparse V gather, as a single fused kernel.
 Inputs are synthetic (seeded, on the device); 4 rotating KV-cache copies
 (4 x 192 MiB > L2) so that no step reads a cache that is still in L2.
 
---impl reference times the CPU oracle of the reference's algorithm (numpy
-port; the reference itself is Python and cannot run on the GPU box) on
-bounded samples of the same workload, on the host cores.
+--impl reference times the reference's own implementation of the step on the
+host cores (its attention.py, installed unmodified into baseline/_ref by
+baseline/install_reference.sh, with its Triton selection replaced by a torch
+compaction), the whole batch per step, with all torch threads; it falls back to
+the numpy port of its algorithm (oracle/) when the reference is not installed.
+The default line also reports, on the GPU, the reference's own torch + Triton
+step and dense GQA decode (this library's kernel and the reference's torch
+bmm) under "gpu_baselines".
 """
 from __future__ import annotations
 
@@ -38,6 +43,7 @@ if REPO not in sys.path:
 
 WORKLOADS = {
     # name: (B, L, Hq, Hk, Hv, D, N, plant)
+    "config1": (1, 4096, 15, 1, 5, 64, 128, 16),  # fp32, the reference's CPU-runnable case
     "config2": (8, 32768, 12, 1, 2, 128, 512, 64),
     "config4": (1, 131072, 12, 1, 2, 128, 1024, 256),
     # the same model with its unmerged key heads, for the dense-GQA baseline (--mode dense)
@@ -199,6 +205,199 @@ def algorithmic_bytes(shape, union_rows: int, mode: str) -> int:
 
 
 # ---------------------------------------------------------------------------
+# The reference itself (noamelata/SAGA, installed unmodified into
+# baseline/_ref by baseline/install_reference.sh)
+# ---------------------------------------------------------------------------
+
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def load_reference():
+    """The reference's attention module from baseline/_ref, or None when the
+    reference is not installed. Its Triton selection kernel is replaced by
+    torch_threshold_topk (the Triton kernel needs a GPU); everything else is
+    the reference's own code."""
+    if not os.path.exists(os.path.join(REF_DIR, "attention", "attention.py")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    import importlib
+    A = importlib.import_module("attention.attention")
+    if os.path.abspath(os.path.dirname(A.__file__)) != os.path.join(REF_DIR, "attention"):
+        raise RuntimeError(f"attention.attention resolved to {A.__file__}, not the installed reference")
+    return A
+
+
+def torch_threshold_topk(x, k: int, threshold):
+    """torch restatement of the reference's threshold_topk_fast
+    (triton_atopn.py:59-113) for CPU tensors: per row, the elements with
+    x > threshold (strict, fp32 compare, triton_atopn.py:42) compacted into k
+    slots in ascending position order; padding vals = -inf, idx = 0
+    (triton_atopn.py:82-84). When more than k pass, the k lowest positions are
+    kept (the Triton kernel keeps an arbitrary k)."""
+    import torch
+    shape = x.shape
+    L = shape[-1]
+    xf = x.reshape(-1, L)
+    R = xf.shape[0]
+    t = threshold.reshape(-1).to(torch.float32)
+    if t.numel() != R:
+        t = t.repeat((R + t.numel() - 1) // t.numel())[:R]
+    passing = xf.to(torch.float32) > t[:, None]
+    rank = passing.cumsum(-1) - 1
+    keep = passing & (rank < k)
+    rows, cols = keep.nonzero(as_tuple=True)
+    vals = torch.full((R, k), float("-inf"), dtype=x.dtype)
+    idx = torch.zeros((R, k), dtype=torch.int64)
+    slot = rank[rows, cols]
+    vals[rows, slot] = xf[rows, cols]
+    idx[rows, slot] = cols
+    return vals.reshape(shape[:-1] + (k,)), idx.reshape(shape[:-1] + (k,))
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def make_cpu_inputs(shape, seed: int, dtype_name: str):
+    """The workload's seeded synthetic tensors on the host (torch CPU)."""
+    import torch
+    B, L, Hq, Hk, Hv, D, N, plant = shape
+    g = torch.Generator().manual_seed(seed)
+    dt = {"bf16": torch.bfloat16, "fp32": torch.float32}[dtype_name]
+    s = 0.5 if dtype_name == "bf16" else 1.0
+    q0 = torch.randn(B, Hq, 1, D, generator=g) * s
+    q1 = 0.9 * q0 + math.sqrt(1 - 0.81) * torch.randn(B, Hq, 1, D, generator=g) * s
+    k = torch.randn(B, Hk, L, D, generator=g) * s
+    G = Hq // Hk
+    for kk in range(Hk):
+        qh = q0[:, kk * G, 0]
+        qhat = qh / qh.norm(dim=-1, keepdim=True)
+        pos = torch.randint(0, L, (B, plant), generator=g)
+        k[torch.arange(B)[:, None], kk, pos] += 4.0 * qhat[:, None, :]
+    v = torch.randn(B, Hv, L, D, generator=g) * s
+    return q0.to(dt), q1.to(dt), k.to(dt), v.to(dt)
+
+
+def reference_cpu(shape, steps: int, warmup: int, dtype_name: str = "bf16", budget_s: float = 60.0):
+    """Time the reference's own amortized step (attention.py:192-209) on the
+    host cores, all torch threads, on the whole batch of the workload per step.
+    Returns the cpu_baseline dict, or None when the reference is absent."""
+    import torch
+    A = load_reference()
+    if A is None:
+        return None
+    A._threshold_topk_triton = torch_threshold_topk
+    B, L, Hq, Hk, Hv, D, N, plant = shape
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    q0, q1, k, v = make_cpu_inputs(shape, 0, dtype_name)
+    with torch.no_grad():
+        A.init_amortized_threshold_tensor("cpu", A.MAX_LAYERS, B * Hq)
+        A.approx_top_n_attention_amortized_cal(q0, k, v, None, top_n_attention=N, layer_idx=0)
+        for _ in range(max(1, warmup)):
+            A.approx_top_n_attention_amortized(q1, k, v, None, top_n_attention=N, layer_idx=0)
+        times = []
+        t_start = time.perf_counter()
+        for _ in range(max(1, steps)):
+            t0 = time.perf_counter()
+            A.approx_top_n_attention_amortized(q1, k, v, None, top_n_attention=N, layer_idx=0)
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    t = statistics.median(times)
+    return {"value": B / t, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "ms_per_step": round(t * 1e3, 3), "os_cpu_count": cores, "torch_threads": torch.get_num_threads(),
+            "cpu_model": cpu_model(),
+            "sample": f"the whole batch ({B} sequences) per step, {len(times)} steps, median; the reference's "
+                      f"approx_top_n_attention_amortized from baseline/_ref in {dtype_name} on CPU tensors, "
+                      f"its Triton selection replaced by a torch compaction (bench.torch_threshold_topk)"}
+
+
+def graph_ms(torch, stream, fns, steps: int) -> float:
+    """Device ms per call of the step functions `fns` (already warmed up),
+    replayed from one CUDA graph that holds one call of each."""
+    with torch.cuda.stream(stream):
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for f in fns:
+                f()
+        for _ in range(3):
+            graph.replay()
+        stream.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = max(1, steps // len(fns))
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * len(fns))
+    del graph
+    return ms
+
+
+def gpu_baselines(torch, ops, shape, dev, caches, steps: int):
+    """On this GPU, beside the timed step: the reference's own GPU path (its
+    attention.py with the Triton selection kernel, from baseline/_ref) on the
+    same caches, and dense GQA decode of the same model with its unmerged key
+    heads (Hk = Hv) by this library's dense kernel and by the reference's
+    full_einsum_forward (torch bmm). Every step replays from a CUDA graph over
+    rotating caches larger than L2; no torch.compile."""
+    B, L, Hq, Hk, Hv, D, N, _ = shape
+    out = {}
+    stream = torch.cuda.Stream(device=dev)
+    A = load_reference()
+    if A is not None:
+        try:
+            copies = len(caches)
+            with torch.cuda.stream(stream):
+                A.init_amortized_threshold_tensor(dev, A.MAX_LAYERS, B * Hq)
+                for c in range(copies):
+                    A.approx_top_n_attention_amortized_cal(caches[c][0], caches[c][2], caches[c][3], None,
+                                                           top_n_attention=N, layer_idx=c)
+                fns = [(lambda c=c: A.approx_top_n_attention_amortized(caches[c][1], caches[c][2], caches[c][3], None,
+                                                                      top_n_attention=N, layer_idx=c))
+                       for c in range(copies)]
+                for f in fns:  # Triton compiles here
+                    f()
+            out["reference_atopn_us"] = round(1e3 * graph_ms(torch, stream, fns, steps), 3)
+        except Exception as e:  # the reference's GPU path is a reported baseline only
+            out["reference_atopn_error"] = f"{type(e).__name__}: {e}"[:300]
+    # dense GQA of the unmerged model (the reference's baseline, eval.md:60-65)
+    gshape = (B, L, Hq, Hv, Hv, D, N, 0)
+    gq = [make_device_inputs(torch, gshape, dev, seed=100 + c) for c in range(2)]
+    with torch.cuda.stream(stream):
+        fns = [(lambda c=c: ops.dense_decode(gq[c][1], gq[c][2], gq[c][3], None)) for c in range(2)]
+        for f in fns:
+            f()
+    out["dense_gqa_us"] = round(1e3 * graph_ms(torch, stream, fns, steps), 3)
+    if A is not None:
+        with torch.cuda.stream(stream):
+            fns = [(lambda c=c: A.full_einsum_forward(gq[c][1], gq[c][2], gq[c][3], None)) for c in range(2)]
+            for f in fns:
+                f()
+        out["reference_dense_gqa_us"] = round(1e3 * graph_ms(torch, stream, fns, steps), 3)
+    out["dense_gqa_heads"] = [Hq, Hv, Hv]
+    out["how"] = ("CUDA graphs of the steps over rotating caches (> L2); the reference from baseline/_ref "
+                  "(attention.py + triton_atopn.py), its amortized step on this line's caches, without "
+                  "torch.compile and without the KV append")
+    del gq
+    torch.cuda.synchronize()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's algorithm)
 # ---------------------------------------------------------------------------
 
@@ -255,12 +454,20 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_baseline(shape, args.steps, budget_s=max(20.0, 0.5 * args.steps))
+        dtn = "fp32" if args.workload == "config1" else "bf16"
+        cb = reference_cpu(shape, args.steps, args.warmup, dtn, budget_s=max(60.0, 3.0 * args.steps))
+        if cb is None:  # the reference is not installed: the numpy port of its algorithm
+            cb = cpu_baseline(shape, args.steps, budget_s=max(20.0, 0.5 * args.steps))
         line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": unit, "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / cb["value"],
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * B / cb["value"] if cb["kind"] == "reference"
+                else 1e3 / cb["value"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtn,
                 "data": "synthetic", "config": config, "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        if args.workload != "config1":  # the CPU-runnable case beside it
+            c1 = reference_cpu(WORKLOADS["config1"], 20, 3, "fp32", budget_s=20.0)
+            if c1 is not None:
+                line["config1_cpu"] = c1
         print(json.dumps(line))
         return
 
@@ -306,6 +513,14 @@ def main():
                 r = b * Hq + h
                 s.update(sel[r, :int(cnt[r])].tolist())
             union += len(s)
+    overflow_rows = int((diag["count"].cpu() > min(2 * N, L)).sum())
+    if args.mode != "atopn":  # the launches of the timed mode
+        d2 = {}
+        if args.mode == "dense":
+            ops.dense_decode(q1, caches[0][2], caches[0][3], None, diag=d2)
+        else:
+            ops.atopn_calibrate(q1, caches[0][2], caches[0][3], None, thrs[0].clone(), N, diag=d2)
+        diag["launches"] = d2["launches"]
     launches_per_step = len(diag["launches"])
     ops.read_status(dev)
 
@@ -411,6 +626,9 @@ def main():
     barrier()
     ms_e2e = max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
 
+    baselines = None
+    if world == 1 and args.workload in ("config2", "config3_layer", "config5_layer") and args.mode == "atopn":
+        baselines = gpu_baselines(torch, ops, shape, dev, caches, min(400, max(40, args.steps)))
     if sd is not None:  # unmap the peers' workspaces once every rank is done with them
         barrier()
         sd.close()
@@ -436,9 +654,18 @@ def main():
                 "roofline": roofline, "clocks": clocks,
                 "gpu_launches": steps_timed * launches_per_step,
                 "kernels_per_step": diag["launches"], "status": status,
+                "overflow_rows": overflow_rows, "rows": B * Hq,
                 "value_rows_union_per_step": union}
+        if baselines is not None:
+            baselines["atopn_us"] = round(ms * 1e3, 3)
+            dense = min([x for x in (baselines.get("dense_gqa_us"), baselines.get("reference_dense_gqa_us")) if x])
+            baselines["atopn_speedup_vs_faster_dense"] = round(dense / (ms * 1e3), 3)
+            if baselines.get("reference_atopn_us"):
+                baselines["speedup_vs_reference_gpu"] = round(baselines["reference_atopn_us"] / (ms * 1e3), 3)
+            line["gpu_baselines"] = baselines
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(shape, steps=3)
+            cb = reference_cpu(shape, 3, 1, "bf16", budget_s=30.0)
+            line["cpu_baseline"] = cb if cb is not None else cpu_baseline(shape, steps=3)
         print(json.dumps(line))
     if world > 1:
         del graph

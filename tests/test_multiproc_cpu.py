@@ -60,3 +60,21 @@ def test_replica_host_logic_two_ranks():
         assert set(seeds[0]).isdisjoint(seeds[1])  # each rank decodes its own inputs
     b = _bench()
     assert b.job_throughput(8, 2, 0.06) == pytest.approx(16 / 0.06e-3)
+
+
+def test_reference_arm_compaction_matches_the_oracle_selection():
+    """bench.torch_threshold_topk, the torch stand-in for the reference's
+    Triton selection in the CPU reference arm, keeps x > t in ascending
+    position order with -inf / 0 padding, exactly as the oracle's restatement
+    of triton_atopn.py does (the K lowest positions on overflow)."""
+    import numpy as np
+    from oracle import atopn_oracle as O
+    b = _bench()
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(7, 3000, generator=g).to(torch.bfloat16)
+    t = torch.randn(7, generator=g) * 0.4 + 1.2
+    t[3] = -10.0  # every position passes: overflow, the 64 lowest kept
+    vals, idx = b.torch_threshold_topk(x, 64, t)
+    ov, oi, _, _ = O.threshold_select(x.float().numpy(), t.numpy(), 64)
+    np.testing.assert_array_equal(idx.numpy(), oi)
+    np.testing.assert_array_equal(vals.float().numpy(), ov)
