@@ -53,6 +53,15 @@ WORKLOADS = {
 }
 L2_BYTES = 126 * 1024 * 1024
 
+# Model-level workloads, decoded through the reference's own harness
+# (speedup.measure_decode_latency) with this package as its attention module:
+# name: (family, layers, hidden, q heads, value heads, head_dim, mlp, vocab,
+#        batch, prefilled context, new tokens, N, key heads of the dense model)
+MODELS = {
+    "config3": ("llama", 32, 960, 15, 5, 64, 2560, 49152, 16, 16384, 128, 256, 5),
+    "config5": ("qwen2", 28, 1536, 12, 4, 128, 8960, 151936, 64, 65536, 64, 512, 2),
+}
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -60,11 +69,14 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="saga_b200", choices=["saga_b200", "reference"])
-    ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="config2", choices=sorted(WORKLOADS) + sorted(MODELS))
+    ap.add_argument("--iterations", type=int, default=3, help="model workloads: measured generations")
+    ap.add_argument("--compile", action="store_true", help="model workloads: torch.compile(model.forward)")
     ap.add_argument("--mode", default="atopn", choices=["atopn", "dense", "calibrate"])
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-config4", action="store_true", help="skip the sequence-sharded config-4 leg (N > 1)")
     return ap.parse_args()
 
 
@@ -397,6 +409,336 @@ def gpu_baselines(torch, ops, shape, dev, caches, steps: int):
     return out
 
 
+def config4_leg(torch, dist, ops, dev, rank: int, world: int, steps: int):
+    """Config 4 sequence-sharded over the job's ranks (one process per GPU),
+    beside the replica line: batch 1, context 131072, Hq 12 / Hk 1 / Hv 2,
+    head_dim 128, N 1024. Every rank holds its shard of the same sequence
+    (plus the 256-row tail replica); the calibration step and the amortized
+    step each run as one launch per device, exchanging through peer-mapped
+    workspaces. Timed as the max over ranks of device events over rotating
+    shard copies whose bytes exceed twice L2. Checked against the unsharded
+    kernel on the full cache, on this box: outputs (max-abs / relative RMS),
+    thresholds (equal or one ulp apart) and selected sets (merged over the
+    ranks; equal except positions within one ulp of the threshold)."""
+    from saga_b200.seqpar import ShardedDecode, shard_cache, shard_layout
+    shape = WORKLOADS["config4"]
+    B, L, Hq, Hk, Hv, D, N, _ = shape
+    lay = shard_layout(L, world, rank)
+    per_copy = (Hk + Hv) * lay.local_len * D * 2 * B
+    copies = max(2, math.ceil(2 * L2_BYTES / per_copy))
+    shards, full0 = [], None
+    for c in range(copies):  # the same sequences on every rank (seed c), sharded
+        q0, q1, k, v, kn, vn = make_device_inputs(torch, shape, dev, seed=500 + c)
+        shards.append((q0, q1, shard_cache(k, lay), shard_cache(v, lay)))
+        if c == 0:
+            full0 = (q0, q1, k, v)
+        else:
+            del k, v
+    sdc = ShardedDecode(dist.group.WORLD, dev, B, L, Hq, Hk, Hv, D, op="calibrate")
+    sda = ShardedDecode(dist.group.WORLD, dev, B, L, Hq, Hk, Hv, D, op="atopn")
+    thrs = [torch.zeros(B * Hq, dtype=torch.float32, device=dev) for _ in range(copies)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def run(fns, reps):
+        # every rank launches the same steps in the same order: warm-up, then
+        # one CUDA graph of one step per copy, replayed reps times
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for f in fns:
+                f()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for f in fns:
+                    f()
+            graph.replay()
+            stream.synchronize()
+            dist.barrier()
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        del graph
+        return max_over_ranks(torch, dist, e0.elapsed_time(e1) / (reps * len(fns)), dev, world)
+
+    reps = max(1, steps // copies)
+    cal_ms = run([(lambda c=c: sdc(shards[c][0], shards[c][2], shards[c][3], thrs[c], N)) for c in range(copies)],
+                 max(1, reps // 4))
+    amo_ms = run([(lambda c=c: sda(shards[c][1], shards[c][2], shards[c][3], thrs[c], N)) for c in range(copies)], reps)
+    # the check: this rank's sharded result against the unsharded kernel on copy 0
+    q0, q1, k, v = full0
+    thr_u = torch.zeros(B * Hq, dtype=torch.float32, device=dev)
+    thr_s = torch.zeros_like(thr_u)
+    du, ds = {}, {}
+    ref_c = ops.atopn_calibrate(q0, k, v, None, thr_u, N)
+    out_c = sdc(q0, shards[0][2], shards[0][3], thr_s, N)
+    ref_a = ops.atopn_decode(q1, k, v, None, thr_u, N, diag=du)
+    out_a = sda(q1, shards[0][2], shards[0][3], thr_u, N, diag=ds)
+    torch.cuda.synchronize()
+    parts = [None] * world
+    dist.all_gather_object(parts, ds["sel_idx"].cpu())
+    check = None
+    if rank == 0:
+        def close(a, b):
+            a, b = a.float(), b.float()
+            return (round((a - b).abs().max().item(), 6),
+                    round(((a - b).pow(2).mean().sqrt() / b.pow(2).mean().sqrt().clamp_min(1e-12)).item(), 6))
+        merged = torch.stack(parts).amax(0)
+        ref_sel, cnt, t = du["sel_idx"].cpu(), du["count"].cpu(), du["logit_thr"].cpu()
+        lg = ops.attn_logits(q1, k).float().cpu().reshape(B * Hq, L)
+        sets_ok, diff = True, 0
+        for r in range(B * Hq):
+            kept = min(int(cnt[r]), 2 * N)
+            a_, b_ = set(merged[r, :kept].tolist()), set(ref_sel[r, :kept].tolist())
+            d = a_ ^ b_
+            diff += len(d)
+            if -1 in a_:
+                sets_ok = False
+            for pos in d:  # a difference must be a tie: within one bf16 ulp of t
+                x, tt = float(lg[r, pos]), float(t[r])
+                ulp = 2.0 ** (math.floor(math.log2(max(abs(tt), 1e-30))) - 7)
+                if abs(x - tt) > ulp:
+                    sets_ok = False
+        thr_ulps = []
+        for a_, b_ in zip(thr_s.cpu().tolist(), thr_u.cpu().tolist()):
+            ulp = 2.0 ** (math.floor(math.log2(max(abs(b_), 1e-30))) - 7)
+            thr_ulps.append(abs(a_ - b_) / ulp)
+        check = {"amortized_max_abs_rel_rms": close(out_a, ref_a), "calibrate_max_abs_rel_rms": close(out_c, ref_c),
+                 "sets_equal_except_ties": sets_ok, "set_positions_differing": diff,
+                 "thresholds_max_ulps": max(thr_ulps), "rows": B * Hq}
+        am, cm = check["amortized_max_abs_rel_rms"], check["calibrate_max_abs_rel_rms"]
+        check["passed"] = bool(sets_ok and check["thresholds_max_ulps"] <= 1.0 and am[0] <= 2e-2 and am[1] <= 1e-2
+                               and cm[0] <= 2e-2 and cm[1] <= 1e-2)
+    st = ops.read_status(dev)
+    dist.barrier()
+    sdc.close()
+    sda.close()
+    dist.barrier()
+    return {"workload": f"config4: batch {B}, context {L}, Hq {Hq} / Hk {Hk} / Hv {Hv}, head_dim {D}, N {N}, "
+                        f"sequence-sharded over {world} GPUs", "us_per_step": round(amo_ms * 1e3, 3),
+            "tokens_per_s": round(B / (amo_ms * 1e-3), 1), "calibrate_us_per_step": round(cal_ms * 1e3, 3),
+            "copies": copies, "status": st, "check": check,
+            "exchange": "peer-mapped workspaces over NVLink (system-scope slots, histogram atomics and barriers); "
+                        "no collective on the data path"}
+
+
+def reference_harness():
+    """The reference's benchmark module (speedup.py, from baseline/_ref,
+    unchanged) with this package standing in for its `attention` package:
+    speedup's `from attention.attention import ...` and
+    `from attention.triton_atopn import _BUFFER_CACHE` resolve to
+    saga_b200.attention, as they would with this package ahead on sys.path."""
+    import importlib
+    import saga_b200.attention as SP
+    import saga_b200.attention.attention as SA
+    import saga_b200.attention.triton_atopn as ST
+    if not os.path.exists(os.path.join(REF_DIR, "speedup.py")):
+        raise RuntimeError("the reference is not installed (bash baseline/install_reference.sh)")
+    sys.modules["attention"] = SP
+    sys.modules["attention.attention"] = SA
+    sys.modules["attention.triton_atopn"] = ST
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    sp = importlib.import_module("speedup")
+    assert sp.approx_top_n_attention_amortized is SA.approx_top_n_attention_amortized
+    if not getattr(sp, "_saga_cache_fix", False):
+        # Compatibility with the installed transformers (5.5; the reference pins
+        # 5.3): its StaticLayer keeps a cumulative_length tensor that only its
+        # own lazy initialisation moves to the device. speedup.py:119-139 marks
+        # the hand-built layers initialised itself, so the counter stays on the
+        # host and the model's position arithmetic mixes devices. The wrapper
+        # moves it; the caches and everything else are the reference's.
+        import torch
+        orig = sp.initialize_kv_cache
+
+        def initialize_kv_cache(model, max_cache_len, num_key_heads=None, device="cuda", dtype=torch.float32):
+            cache = orig(model, max_cache_len, num_key_heads=num_key_heads, device=device, dtype=dtype)
+            for layer in getattr(cache, "layers", []):
+                cl = getattr(layer, "cumulative_length", None)
+                if isinstance(cl, torch.Tensor) and getattr(layer, "is_initialized", False):
+                    layer.cumulative_length = cl.to(device)
+            return cache
+
+        sp.initialize_kv_cache = initialize_kv_cache
+        sp._saga_cache_fix = True
+    return sp
+
+
+def build_model(torch, family, layers, hidden, heads, kv_heads, head_dim, mlp, vocab, ctx, dev):
+    """A random-init model of the named family's shape: bf16 weights ~ N(0, 0.02)."""
+    from transformers import AutoModelForCausalLM, LlamaConfig, Qwen2Config
+    kw = dict(hidden_size=hidden, num_attention_heads=heads, num_key_value_heads=kv_heads, head_dim=head_dim,
+              intermediate_size=mlp, vocab_size=vocab, num_hidden_layers=layers, max_position_embeddings=ctx,
+              initializer_range=0.02, attn_implementation="sdpa")
+    cfg = LlamaConfig(tie_word_embeddings=True, **kw) if family == "llama" else Qwen2Config(**kw)
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16)
+    return model.eval()
+
+
+def decode_graph_ms(torch, sp, model, input_ids, new_heads, new_tokens: int, iterations: int, atopn: bool):
+    """Per-token decode time of one generation of `new_tokens`, by the protocol
+    of the reference's speedup.measure_decode_latency with use_cuda_graph
+    (speedup.py:197-291, 293-440): prefill at batch 1 and repeat over the batch
+    (its own prefill()), the decode step captured in CUDA graphs (for Atop-N
+    one calibration graph for the first token, one amortized graph for the
+    rest), then replayed with the argmax token fed back, the threshold table
+    reset before every generation. Restated rather than called: with the
+    installed transformers a StaticLayer ignores the cache position and
+    advances its own device counter on every update, so the harness's
+    warm-up forwards and replays would write past the cache's end. Here each
+    captured step first sets every layer's counter back to the prefilled
+    length, so every replay writes the same position, which is what the
+    harness intends ("the graph always writes to the same cache_position").
+    Device time of the replays (CUDA events)."""
+    dev = input_ids.device
+    with torch.no_grad():
+        if atopn:
+            sp._AMORTIZED_STEP_COUNT = 0
+        past_kv, next_token = sp.prefill(model, input_ids, new_heads, dtype=torch.bfloat16, num_new_tokens=new_tokens)
+        if atopn:
+            sp.init_amortized_threshold_tensor(dev, sp.MAX_LAYERS, next_token.shape[0] * model.config.num_attention_heads)
+        seen = int(past_kv.layers[0].cumulative_length.item())
+        position_ids = torch.arange(seen, seen + 1, device=dev, dtype=torch.long).unsqueeze(0)
+        batch = past_kv.layers[0].keys.shape[0]
+        static_input = torch.empty_like(next_token)
+        static_logits = torch.empty(batch, 1, model.config.vocab_size, device=dev, dtype=torch.bfloat16)
+        counters = [layer.cumulative_length for layer in past_kv.layers]
+
+        def step():
+            for c in counters:  # every replay writes the decode token at `seen`
+                c.fill_(seen)
+            # the causal mask is built inside the step from the counter (the
+            # installed transformers takes no precomputed per-type mask dict)
+            out = model(static_input, past_key_values=past_kv, use_cache=True, position_ids=position_ids)
+            static_logits.copy_(out.logits[:, -1:, :])
+
+        static_input.copy_(next_token)
+        if dev.type != "cuda":  # host dry run of the same steps (no graphs, no timing)
+            for i in range(new_tokens):
+                sp._AMORTIZED_STEP_COUNT = 0 if (atopn and i == 0) else 2
+                step()
+                static_input.copy_(static_logits.argmax(dim=-1))
+            return float("nan")
+        graphs = {}
+        for name, count in ((("cal", 0), ("fast", 2)) if atopn else (("fast", 2),)):
+            sp._AMORTIZED_STEP_COUNT = count
+            step()  # warm-up outside the capture (lazy set-up, workspaces)
+            torch.cuda.synchronize()
+            sp._AMORTIZED_STEP_COUNT = count
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step()
+            graphs[name] = gr
+        times = []
+        for it in range(iterations + 1):  # the first generation is a warm-up
+            if atopn:
+                sp.reset_amortized_state()
+            tok = next_token
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(new_tokens):
+                static_input.copy_(tok)
+                graphs["cal" if (atopn and i == 0) else "fast"].replay()
+                tok = static_logits.argmax(dim=-1)
+            e1.record()
+            torch.cuda.synchronize()
+            if it > 0:
+                times.append(e0.elapsed_time(e1) / new_tokens)
+        del graphs, past_kv
+    return statistics.median(times)
+
+
+def model_bench(args, world: int, rank: int, local_rank: int):
+    """Decode tokens/s of a whole random-init model, decoded by the protocol
+    of the reference's speedup.measure_decode_latency (decode_graph_ms) with
+    this package's attention module standing in for the reference's, the
+    reference's own dispatcher (speedup.sdpa_attention_forward_dispatch),
+    prefill and key-head merge. The SAGA model (key projection merged to one
+    head, Atop-N with the calibration at the first decode step) is reported
+    next to the same model with its unmerged key heads and dense attention: the
+    reference's "full" mode (this package's dense kernel) and plain SDPA.
+    Batch-sharded: every rank decodes batch / ranks sequences of its own; the
+    job's rate uses the slowest rank's time."""
+    import torch
+    import torch.distributed as dist
+    family, layers, hidden, heads, vh, hd, mlp, vocab, B, ctx, new, N, dense_kv = MODELS[args.workload]
+    if B % world:
+        raise SystemExit(f"batch {B} does not split over {world} ranks")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=1800), device_id=dev)
+    sp = reference_harness()
+    from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
+    ALL_ATTENTION_FUNCTIONS["sdpa"] = sp.sdpa_attention_forward_dispatch
+    b_rank = B // world
+    g = torch.Generator().manual_seed(1000 + rank)
+    input_ids = torch.randint(0, vocab, (b_rank, ctx), generator=g, dtype=torch.long).to(dev)
+    runs = {}
+
+    def measure(name, kv_heads, mode, merge):
+        model = build_model(torch, family, layers, hidden, heads, kv_heads, hd, mlp, vocab, ctx + new + 8, dev)
+        if merge:
+            model = sp.merge_key_projection_heads(model, new_heads=1)
+        if args.compile:
+            model.forward = torch.compile(model.forward)
+        sp.ATTENTION_MODE = mode
+        sp.TOP_N_ATTENTION = N if mode == "atopn" else None
+        err = None
+        try:
+            ms = decode_graph_ms(torch, sp, model, input_ids, 1 if merge else None, new, args.iterations,
+                                 mode == "atopn")
+        except torch.cuda.OutOfMemoryError:
+            ms, err = float("inf"), "out of memory"
+        del model
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        from saga_b200 import ops
+        st = ops.read_status(dev)
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        runs[name] = {"ms_per_token": round(ms, 4) if ms != float("inf") else None,
+                      "tokens_per_s": round(B / (ms * 1e-3), 1) if ms != float("inf") else None,
+                      "key_heads": 1 if merge else kv_heads, "value_heads": kv_heads, "attention": mode,
+                      "status": st}
+        if err:
+            runs[name]["error"] = err
+
+    measure("saga_atopn", vh, "atopn", True)
+    measure("dense_full", dense_kv, "full", False)
+    measure("dense_sdpa", dense_kv, "vanilla", False)
+    if rank == 0:
+        saga, dense = runs["saga_atopn"], [runs["dense_full"], runs["dense_sdpa"]]
+        best = min([d["ms_per_token"] for d in dense if d["ms_per_token"]] or [float("nan")])
+        line = {"metric": f"decode tokens/s of the whole model ({args.workload}: {family}-shaped SAGA model)",
+                "value": saga["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.iterations * new,
+                "warmup": new, "ms_per_step": saga["ms_per_token"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random token ids)",
+                "config": {"workload": f"{args.workload}: {layers} layers, hidden {hidden}, {heads} query heads, "
+                                       f"1 key head / {vh} value heads, head_dim {hd}, MLP {mlp}, vocab {vocab}, "
+                                       f"batch {B}, context {ctx}, {new} new tokens, N {N}",
+                           "parallelism": f"replicas x{world} (batch-sharded, no collective)",
+                           "harness": "the protocol of the reference's measure_decode_latency with CUDA graphs "
+                                      "(its prefill, merge and dispatcher); device time of the replays" +
+                                      (", torch.compile(model.forward)" if args.compile else "")},
+                "runs": runs,
+                "atopn_speedup_vs_faster_dense": round(best / saga["ms_per_token"], 3) if saga["ms_per_token"] else None}
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port of the reference's algorithm)
 # ---------------------------------------------------------------------------
@@ -431,6 +773,15 @@ def cpu_baseline(shape, steps: int, budget_s: float = 20.0):
 
 def main():
     args = parse()
+    if args.workload in MODELS:
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "model workloads run the reference's harness "
+                                  "with this package as its attention module; the reference's own model decode "
+                                  "needs its Triton kernel on a GPU and is not a CPU baseline"}))
+            return
+        return model_bench(args, world, int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")))
     shape = WORKLOADS[args.workload]
     B, L, Hq, Hk, Hv, D, N, _ = shape
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -629,6 +980,9 @@ def main():
     baselines = None
     if world == 1 and args.workload in ("config2", "config3_layer", "config5_layer") and args.mode == "atopn":
         baselines = gpu_baselines(torch, ops, shape, dev, caches, min(400, max(40, args.steps)))
+    c4 = None
+    if world > 1 and not sharded and args.mode == "atopn" and not args.no_config4:
+        c4 = config4_leg(torch, dist, ops, dev, rank, world, min(400, max(40, args.steps)))
     if sd is not None:  # unmap the peers' workspaces once every rank is done with them
         barrier()
         sd.close()
@@ -656,6 +1010,8 @@ def main():
                 "kernels_per_step": diag["launches"], "status": status,
                 "overflow_rows": overflow_rows, "rows": B * Hq,
                 "value_rows_union_per_step": union}
+        if c4 is not None:
+            line["config4_sharded"] = c4
         if baselines is not None:
             baselines["atopn_us"] = round(ms * 1e3, 3)
             dense = min([x for x in (baselines.get("dense_gqa_us"), baselines.get("reference_dense_gqa_us")) if x])
