@@ -119,8 +119,10 @@ typedef struct SagaAttnArgs {
    * devices through their workspaces: shard_workspaces[s] is shard s's
    * workspace mapped into this device (peer memory over NVLink), and
    * shard_workspaces[shard] == workspace. All shards must use the same
-   * shapes and nsel. Every shard writes the full output. Supported for
-   * saga_atopn_decode and saga_dense_decode. shards = 0 or 1: not sharded. */
+   * shapes and nsel. Every shard writes the full output (and, for the
+   * calibration, its own copy of every row's threshold). Supported for
+   * saga_atopn_decode, saga_atopn_calibrate and saga_dense_decode.
+   * shards = 0 or 1: not sharded. */
   int32_t nsel;        /* 0 = L */
   int32_t pos_offset;  /* added to the positions written to sel_idx_out */
   int32_t shards;

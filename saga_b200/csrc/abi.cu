@@ -84,8 +84,8 @@ int check_attn(const SagaAttnArgs* a, int op) {
   if (a->shards > 1) {
     if (a->shards > 8 || a->shard < 0 || a->shard >= a->shards)
       return fail(SAGA_ERR_INVALID, "shards in [1, 8] and 0 <= shard < shards required");
-    if (op != SAGA_OP_ATOPN_DECODE && op != SAGA_OP_DENSE_DECODE)
-      return fail(SAGA_ERR_UNSUPPORTED, "sequence sharding supports the decode and dense ops");
+    if (op != SAGA_OP_ATOPN_DECODE && op != SAGA_OP_DENSE_DECODE && op != SAGA_OP_ATOPN_CALIBRATE)
+      return fail(SAGA_ERR_UNSUPPORTED, "sequence sharding supports the decode, calibration and dense ops");
     if (a->dtype == SAGA_FP32 || a->Hq / a->Hk > 16)
       return fail(SAGA_ERR_UNSUPPORTED, "sequence sharding needs the tensor-core path (16-bit, G <= 16)");
     for (int s = 0; s < a->shards; ++s)

@@ -279,6 +279,35 @@ __device__ __forceinline__ bool group_barrier(int* ctr, int target, bool arrive,
   return *smem_flag != 0;
 }
 
+// The same barrier across devices (sequence sharding): the counter lives in
+// one device's memory and every device's CTAs arrive and poll at system scope.
+__device__ __forceinline__ bool group_barrier_sys(int* ctr, int target, int* status, int* smem_flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    atomicAdd_system(ctr, 1);
+    int ok = 1;
+    unsigned long long t0 = 0;
+    for (uint32_t i = 1; ld_acquire_sys(ctr) < target; ++i) {
+      __nanosleep(64);
+      if ((i & 255u) == 0) {
+        const unsigned long long now = globaltimer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kWaitLimitNs) {
+          ok = 0;
+          if (status) atomicOr(status, SAGA_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __threadfence_system();
+    *smem_flag = ok;
+  }
+  __syncthreads();
+  return *smem_flag != 0;
+}
+
 __device__ __forceinline__ void set_status(int* status, int bits) {
   if (status) atomicOr(status, bits);
 }

@@ -94,7 +94,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // The kernel's dynamic shared-memory limit is a per-function, per-device
 // attribute; plans of different shapes may share a kernel, so it only rises.
-static int raise_smem_limit(const void* kfn, int smem) {
+static int raise_smem_limit(const void* kfn, int smem, std::string* err = nullptr) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, int> set_to;
   int dev = 0;
@@ -102,7 +102,14 @@ static int raise_smem_limit(const void* kfn, int smem) {
   std::lock_guard<std::mutex> lock(mu);
   int& cur = set_to[{dev, kfn}];
   if (smem <= cur) return 0;
-  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -1;
+  const cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear it: the caller reports this call's own error
+    if (err)
+      *err = std::string("cudaFuncSetAttribute(") + std::to_string(smem) + " bytes of shared memory): " +
+             cudaGetErrorString(e);
+    return -1;
+  }
   cur = smem;
   return 0;
 }
@@ -191,8 +198,20 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
   int C = std::max(c_fit, std::min(c_par, ntiles));
   int tiles = (ntiles + C - 1) / C;
   C = (ntiles + tiles - 1) / tiles;
+  // The layout is not monotone in C: fewer chunks shrink the exchange staging
+  // at the end of the work area, which lends the P.V weight buffer more rows.
+  // Re-check the final layout and shorten the chunks until it fits.
+  SmemLayout sm = smem_layout(G, a->D, tiles * kTile, es, C * shards, C, tc, ns, ngg);
+  while (sm.total > budget && tiles > 1) {
+    --tiles;
+    C = (ntiles + tiles - 1) / tiles;
+    sm = smem_layout(G, a->D, tiles * kTile, es, C * shards, C, tc, ns, ngg);
+  }
+  if (sm.total > budget) {
+    *err = "shapes need more shared memory than one CTA has";
+    return SAGA_ERR_UNSUPPORTED;
+  }
   const int CL = tiles * kTile;
-  const SmemLayout sm = smem_layout(G, a->D, CL, es, C * shards, C, tc, ns, ngg);
 
   pl->G = G;
   pl->Gv = Gv;
@@ -226,10 +245,7 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
     const int floor_smem = di.smem_per_sm / (max_per_sm + 1) + 1024;
     if (pl->smem < floor_smem) pl->smem = std::min(floor_smem, budget);
   }
-  if (raise_smem_limit(kfn, pl->smem) != 0) {
-    *err = std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(cudaGetLastError());
-    return SAGA_ERR_CUDA;
-  }
+  if (raise_smem_limit(kfn, pl->smem, err) != 0) return SAGA_ERR_CUDA;
   int nb = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kfn, kThreads, pl->smem) != cudaSuccess || nb <= 0) {
     *err = "occupancy query failed";
@@ -312,11 +328,17 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
     p.ctrl_home = p.ctrl;
     p.slot_base[0] = p.slots;
     p.ctrl_peer[0] = p.ctrl;
+    p.stats_peer[0] = p.stats;
+    p.hist_home = p.hist;
     if (shards > 1) {  // every shard's workspace has the same layout
       for (int s2 = 0; s2 < shards; ++s2) {
         uint8_t* w = reinterpret_cast<uint8_t*>(a->shard_workspaces[s2]);
         p.slot_base[s2] = reinterpret_cast<unsigned long long*>(w + pl.ws_part);
         p.ctrl_peer[s2] = reinterpret_cast<int*>(w + pl.ws_ctrl);
+        if (mode == MODE_CALIBRATE) {
+          p.stats_peer[s2] = reinterpret_cast<ChunkStat*>(w + pl.ws_stats);
+          if (s2 == 0) p.hist_home = reinterpret_cast<int*>(w + pl.ws_hist);
+        }
       }
       p.ctrl_home = p.ctrl_peer[0];
     }

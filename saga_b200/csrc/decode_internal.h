@@ -132,7 +132,9 @@ struct DecodeParams {
   // [c % c_local][head][D + 4]; the epoch and completion counters are shard 0's
   int nsel, pos_offset, shards, shard, c_local;
   unsigned long long* slot_base[kMaxShards];
-  int* ctrl_home;               // shard 0's control counters (device tickets)
+  int* ctrl_home;               // shard 0's control counters (device tickets, calibration barriers)
+  ChunkStat* stats_peer[kMaxShards];  // calibration: every shard's chunk statistics [group][c_local][G]
+  int* hist_home;               // calibration: shard 0's histograms (every device adds into them)
   int* ctrl_peer[kMaxShards];   // every shard's control counters (epoch releases)
   int* status;
   long long* trace;

@@ -1806,8 +1806,13 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
     const int n = min(p.nsel - p0, CL);
     const int nw = (n + 31) / 32;
     int* ctrl = p.ctrl + (size_t)g * kCtrlInts;  // this device's counters of the group
-    ChunkStat* stg = p.stats + (size_t)g * C * G;  // [C][G] (calibration)
-    ChunkStat* st = stg + (size_t)j * G;
+    // calibration statistics: this chunk's, and chunk c's of the group (on the
+    // device that owns it when the sequence is sharded)
+    ChunkStat* st = p.stats ? p.stats + ((size_t)g * p.c_local + jl) * G : nullptr;
+    const auto stat = [&](int c, int hl) -> const ChunkStat* {
+      const int owner = SHD ? c / p.c_local : 0;
+      return p.stats_peer[owner] + ((size_t)g * p.c_local + (c - owner * p.c_local)) * G + hl;
+    };
     const int row0 = b * p.Hq + h0;
     const bool tracing = kTrace && p.trace && threadIdx.x == 0 && item == (int)blockIdx.x && blockIdx.x < 1024;
 #define SAGA_TRACE(k) \
@@ -2073,7 +2078,9 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       constexpr int PASSES = KB / 8;
       const int nsel = p.buf_k;  // min(N, L)
       int* hsm = reinterpret_cast<int*>(work);     // [G][256]
-      int* gh = p.hist + (size_t)g * 4 * G * 256;  // [pass][G][256]
+      // the group's histograms [pass][G][256] (shard 0's with sequence sharding)
+      int* gh = p.hist_home + (size_t)g * 4 * G * 256;
+      int* bctrl = SHD ? p.ctrl_home + (size_t)g * kCtrlInts : ctrl;  // barrier counters
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         st[hl].mx = misc->aux[hl];
         misc->i0[hl] = nsel;  // rank wanted within the current key prefix
@@ -2091,8 +2098,12 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
           if (match) atomicAdd(&hsm[hl * 256 + ((key >> shift) & 255u)], 1);
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < G * 256; i += kThreads)
-          if (hsm[i]) atomicAdd(&gh[(size_t)pass * G * 256 + i], hsm[i]);
+        for (int i = threadIdx.x; i < G * 256; i += kThreads) {
+          if (hsm[i]) {
+            if constexpr (SHD) atomicAdd_system(&gh[(size_t)pass * G * 256 + i], hsm[i]);
+            else atomicAdd(&gh[(size_t)pass * G * 256 + i], hsm[i]);
+          }
+        }
         if (pass == 1) {
           // exp-sum with the global max (attention.py:131-133 softmax)
           for (int hl = warp; hl < G; hl += kWarps) {
@@ -2103,18 +2114,19 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
             if (lane == 0) st[hl].s = s;
           }
         }
-        group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
+        if constexpr (SHD) group_barrier_sys(&bctrl[sync_id++], C, p.status, &misc->flag);
+        else group_barrier(&bctrl[sync_id++], C, true, p.status, &misc->flag);
         if (pass == 0) {
           for (int hl = threadIdx.x; hl < G; hl += kThreads) {
             float M = -INFINITY;
-            for (int c = 0; c < C; ++c) M = nanmax(M, __ldcg(&stg[(size_t)c * G + hl].mx));
+            for (int c = 0; c < C; ++c) M = nanmax(M, __ldcg(&stat(c, hl)->mx));
             misc->m[hl] = M;
           }
         }
         if (pass == 1) {
           for (int hl = threadIdx.x; hl < G; hl += kThreads) {
             float s = 0.f;
-            for (int c = 0; c < C; ++c) s += __ldcg(&stg[(size_t)c * G + hl].s);
+            for (int c = 0; c < C; ++c) s += __ldcg(&stat(c, hl)->s);
             misc->s[hl] = s;
           }
         }
@@ -2135,7 +2147,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         const float pN = Num<T>::round(__fdiv_rn(expf(__fsub_rn(lN, misc->m[hl])), misc->s[hl]));
         misc->t[hl] = lN;
         misc->aux[hl] = pN;
-        if (j == 0 && p.thr_out) p.thr_out[row0 + hl] = pN;
+        if (jl == 0 && p.thr_out) p.thr_out[row0 + hl] = pN;  // every device's own table
       }
       __syncthreads();
       for (int hl = warp; hl < G; hl += kWarps) {
@@ -2160,21 +2172,22 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
           misc->i2[hl] = ce;
         }
       }
-      group_barrier(&ctrl[sync_id++], C, true, p.status, &misc->flag);
+      if constexpr (SHD) group_barrier_sys(&bctrl[sync_id++], C, p.status, &misc->flag);
+      else group_barrier(&bctrl[sync_id++], C, true, p.status, &misc->flag);
       // ties at the N-th probability: the lowest positions fill the set
       for (int hl = threadIdx.x; hl < G; hl += kThreads) {
         int tot_gt = 0;
-        for (int c = 0; c < C; ++c) tot_gt += __ldcg(&stg[(size_t)c * G + hl].cnt);
+        for (int c = 0; c < C; ++c) tot_gt += __ldcg(&stat(c, hl)->cnt);
         const int need = max(0, nsel - tot_gt);
         int eq_pre = 0, pos_pre = 0;
         for (int c = 0; c < j; ++c) {
-          const int ce = __ldcg(&stg[(size_t)c * G + hl].cnt_eq);
-          pos_pre += __ldcg(&stg[(size_t)c * G + hl].cnt) + max(0, min(ce, need - eq_pre));
+          const int ce = __ldcg(&stat(c, hl)->cnt_eq);
+          pos_pre += __ldcg(&stat(c, hl)->cnt) + max(0, min(ce, need - eq_pre));
           eq_pre += ce;
         }
         misc->i2[hl] = max(0, min(misc->i2[hl], need - eq_pre));  // kept ties here
         misc->i3[hl] = max(0, pos_pre);
-        if (j == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
+        if (jl == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
       }
       __syncthreads();
       for (int hl = warp; hl < G; hl += kWarps) {
@@ -2182,7 +2195,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         for (int w = lane; w < nw; w += 32) sel[hl * (CL / 32) + w] |= eqb[hl * (CL / 32) + w];
         __syncwarp();
         if (p.sel_idx_out && misc->i3[hl] < p.sel_ld)
-          warp_write_positions(sel + hl * (CL / 32), nw, p0,
+          warp_write_positions(sel + hl * (CL / 32), nw, p.pos_offset + p0,
                                p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
                                max(0, p.sel_ld - misc->i3[hl]));
       }
@@ -2296,10 +2309,12 @@ const void* pick_d_mode(int D, int mode) {
     if (!TC) return nullptr;
     if (D == 64) {
       if (mode == MODE_AMORTIZED) return decode_kernel_ptr<T, 64, MODE_AMORTIZED, TC, MASK, true>();
+      if (mode == MODE_CALIBRATE) return decode_kernel_ptr<T, 64, MODE_CALIBRATE, TC, MASK, true>();
       if (mode == MODE_DENSE) return decode_kernel_ptr<T, 64, MODE_DENSE, TC, MASK, true>();
       return nullptr;
     }
     if (mode == MODE_AMORTIZED) return decode_kernel_ptr<T, 128, MODE_AMORTIZED, TC, MASK, true>();
+    if (mode == MODE_CALIBRATE) return decode_kernel_ptr<T, 128, MODE_CALIBRATE, TC, MASK, true>();
     if (mode == MODE_DENSE) return decode_kernel_ptr<T, 128, MODE_DENSE, TC, MASK, true>();
     return nullptr;
   } else {

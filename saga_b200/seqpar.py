@@ -12,6 +12,12 @@ exchanges run between the devices through peer-mapped workspaces (NVLink):
 * the global K = min(2N, L) cap;
 * the partial outputs, merged by log-sum-exp;
 * the completion ticket.
+The calibration step (attention.py:173-189) is sharded the same way: every
+device adds its chunks' 256-bin logit-key histograms into shard 0's (system-
+scope atomics over NVLink), the chunks meet at system-scope barriers on shard
+0's counters, and every device reads all chunks' maxima, exp-sums and counts
+from the peers' workspaces; so every shard computes the exact global N-th
+largest probability, the threshold of the whole row.
 No collective library is on the data path; torch.distributed only exchanges
 the workspaces' IPC handles once, at set-up. Every shard ends with the full
 output.
@@ -70,7 +76,9 @@ def shard_cache(cache: torch.Tensor, lay: ShardLayout) -> torch.Tensor:
     tail replica when it is not the last shard (a new contiguous tensor)."""
     own = cache[:, :, lay.offset:lay.offset + lay.own]
     if not lay.replica:
-        return own.contiguous()
+        # a copy even when the slice is already contiguous (B = H = 1): an
+        # append into the shard must not write through to `cache`
+        return own.clone(memory_format=torch.contiguous_format)
     return torch.cat([own, cache[:, :, lay.L - TAIL:]], dim=2).contiguous()
 
 
@@ -91,7 +99,8 @@ class ShardedDecode:
         self.lay = shard_layout(L, self.shards, self.rank)
         self.shape = (B, Hq, Hk, Hv, D)
         self.dtype = dtype
-        self.op = Lib.SAGA_OP_ATOPN_DECODE if op == "atopn" else Lib.SAGA_OP_DENSE_DECODE
+        self.op = {"atopn": Lib.SAGA_OP_ATOPN_DECODE, "dense": Lib.SAGA_OP_DENSE_DECODE,
+                   "calibrate": Lib.SAGA_OP_ATOPN_CALIBRATE}[op]
         probe = self._probe_args()
         nbytes = Lib.lib.saga_workspace_bytes(ctypes.byref(probe), self.op)
         if nbytes == 0:
@@ -148,7 +157,12 @@ class ShardedDecode:
     def __call__(self, q, k_local, v_local, threshold=None, top_n: int = 256, scaling=None,
                  k_new=None, v_new=None, append_pos: int = -1, diag=None):
         """One decode step on this shard. k_local / v_local: [B, H, local_len, D]
-        from shard_cache(). append_pos is global. Returns the full [B, Hq, 1, D]."""
+        from shard_cache(). append_pos is global. Returns the full [B, Hq, 1, D].
+        For the amortized op `threshold` holds the rows' softmax-space
+        thresholds; for the calibration op it receives them (every shard
+        writes its own copy of the whole row set). With `diag`, this shard
+        writes the kept positions of its own chunks (global positions) at their
+        global ranks; the other ranks' slots stay -1."""
         a = ops._attn_args(q, k_local, v_local, None, scaling)
         a.nsel = self.lay.own
         a.pos_offset = self.lay.offset
@@ -159,6 +173,9 @@ class ShardedDecode:
         if self.op == Lib.SAGA_OP_ATOPN_DECODE:
             a.top_n = top_n
             a.thr_in = threshold.data_ptr()
+        elif self.op == Lib.SAGA_OP_ATOPN_CALIBRATE:
+            a.top_n = top_n
+            a.thr_out = threshold.data_ptr()
         if k_new is not None:
             lp = self.lay.local_position(append_pos)
             if lp < 0:
@@ -169,7 +186,9 @@ class ShardedDecode:
         a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
         a.status = ops.status_tensor(self.device).data_ptr()
         if diag is not None:
-            ops._diag_buffers(a, q, min(2 * top_n, self.lay.L), diag)
-        fn = "saga_atopn_decode" if self.op == Lib.SAGA_OP_ATOPN_DECODE else "saga_dense_decode"
+            kk = top_n if self.op == Lib.SAGA_OP_ATOPN_CALIBRATE else 2 * top_n
+            ops._diag_buffers(a, q, min(kk, self.lay.L), diag)
+        fn = {Lib.SAGA_OP_ATOPN_DECODE: "saga_atopn_decode", Lib.SAGA_OP_DENSE_DECODE: "saga_dense_decode",
+              Lib.SAGA_OP_ATOPN_CALIBRATE: "saga_atopn_calibrate"}[self.op]
         Lib.check(getattr(Lib.lib, fn)(ctypes.byref(a), ctypes.c_void_p(ops._stream(q.device))), fn)
         return out

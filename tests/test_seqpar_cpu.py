@@ -49,6 +49,19 @@ def test_shard_cache_rows():
             assert torch.equal(loc[0, 0, lay.own:, 0], torch.arange(L - TAIL, L, dtype=torch.float32))
 
 
+def test_shard_cache_never_aliases_the_full_cache():
+    # B = H = 1: the last shard's slice is already contiguous; an append into
+    # the shard must still leave the full cache as it was
+    L, P = 2048, 2
+    cache = torch.arange(L, dtype=torch.float32).view(1, 1, L, 1).expand(1, 1, L, 4).contiguous()
+    before = cache.clone()
+    for r in range(P):
+        loc = shard_cache(cache, shard_layout(L, P, r))
+        assert loc.is_contiguous()
+        loc.fill_(-1.0)
+    assert torch.equal(cache, before)
+
+
 def test_layout_rejects_uneven_or_tiny_shards():
     with pytest.raises(ValueError):
         shard_layout(1000, 3, 0)
