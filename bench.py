@@ -8,9 +8,14 @@ append of the new token, logits over the reduced key head, threshold
 transform, selection and the sparse V gather, as a single fused kernel.
 
   value      decode tokens/s of the layer, whole job (sum over ranks): B * N_gpus / step time
-  e2e        the same through the public API (saga_b200.ops.atopn_decode) with
-             the step's inputs copied from pinned host memory and its output
-             copied back, inside the timed region
+  e2e        the same through the serving API (saga_b200.ops.DecodeStep: the
+             step's arguments bound once, one C-ABI call per step), with the
+             step's inputs copied from pinned host memory and its output
+             copied back, inside the timed region, the copies on two side
+             streams under the neighbouring steps' kernels; "e2e_serial" the
+             same with every copy and step in order on one stream, and
+             "e2e_per_call" that through the per-call functions
+             (saga_b200.ops.atopn_decode)
   roofline   algorithmic HBM bytes of one step / step time, against the
              measured copy bandwidth (MEASURED_PEAKS.json)
 
@@ -938,44 +943,137 @@ def main():
     ms = max_over_ranks(torch, dist, e0.elapsed_time(e1) / steps_timed, dev, world)
     status = ops.read_status(dev)
 
-    # end to end through the public API with host buffers
-    hq = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, pin_memory=True)
-    hq.copy_(q1.cpu())
-    hkn = caches[0][4].cpu().pin_memory()
-    hvn = caches[0][5].cpu().pin_memory()
+    # End to end with host buffers. Every step copies one pinned host block
+    # (the query and the decode token's key/value rows) into the device block
+    # the step reads, runs the step, and copies the output back to pinned
+    # host memory. Two API levels are timed: the serving API (ops.DecodeStep,
+    # arguments bound once, one C-ABI call per step) as "e2e", and the
+    # per-call functions the reference's module API goes through
+    # (ops.atopn_decode & co., arguments built every call) as "e2e_per_call".
+    nq, nk, nv = B * Hq * D, B * Hk * D, B * Hv * D
+    hin = torch.empty(nq + nk + nv, dtype=torch.bfloat16, pin_memory=True)
+    hin[:nq].copy_(q1.reshape(-1).cpu())
+    hin[nq:nq + nk].copy_(caches[0][4].reshape(-1).cpu())
+    hin[nq + nk:].copy_(caches[0][5].reshape(-1).cpu())
+    din = torch.empty(hin.shape, dtype=hin.dtype, device=dev)
+    qd = din[:nq].view(B, Hq, 1, D)
+    knd = din[nq:nq + nk].view(B, Hk, 1, D)
+    vnd = din[nq + nk:].view(B, Hv, 1, D)
     hout = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, pin_memory=True)
-    h2d = hq.numel() * 2 + hkn.numel() * 2 + hvn.numel() * 2
+    h2d = hin.numel() * 2
     d2h = hout.numel() * 2
     ne = max(copies, args.e2e_steps)
+    bound = None
+    if sd is None:
+        bound = []
+        for c in range(copies):
+            _, _, kc, vc, _, _ = caches[c]
+            if args.mode == "calibrate":
+                bound.append(ops.DecodeStep("calibrate", qd, kc, vc, threshold=thrs[c], top_n=N))
+            else:
+                bound.append(ops.DecodeStep(args.mode, qd, kc, vc, threshold=thrs[c] if args.mode == "atopn" else None,
+                                            top_n=N, k_new=knd, v_new=vnd, append_pos=L - 1))
 
-    def e2e_step(i):
+    def per_call(i):
         _, _, kc, vc, _, _ = caches[i % copies]
-        qd = hq.to(dev, non_blocking=True)
-        knd = hkn.to(dev, non_blocking=True)
-        vnd = hvn.to(dev, non_blocking=True)
         if sd is not None:
-            o = sd(qd, kc, vc, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
-        elif args.mode == "atopn":
-            o = ops.atopn_decode(qd, kc, vc, None, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
-        elif args.mode == "dense":
-            o = ops.dense_decode(qd, kc, vc, None, k_new=knd, v_new=vnd, append_pos=L - 1)
-        else:
-            o = ops.atopn_calibrate(qd, kc, vc, None, thrs[i % copies], N)
-        hout.copy_(o, non_blocking=True)
+            return sd(qd, kc, vc, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
+        if args.mode == "atopn":
+            return ops.atopn_decode(qd, kc, vc, None, thrs[i % copies], N, k_new=knd, v_new=vnd, append_pos=L - 1)
+        if args.mode == "dense":
+            return ops.dense_decode(qd, kc, vc, None, k_new=knd, v_new=vnd, append_pos=L - 1)
+        return ops.atopn_calibrate(qd, kc, vc, None, thrs[i % copies], N)
 
-    for i in range(3):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    barrier()
-    f0 = torch.cuda.Event(enable_timing=True)
-    f1 = torch.cuda.Event(enable_timing=True)
-    f0.record()
-    for i in range(ne):
-        e2e_step(i)
-    f1.record()
-    torch.cuda.synchronize()
-    barrier()
-    ms_e2e = max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
+    def e2e_ms(run):
+        def e2e_step(i):
+            din.copy_(hin, non_blocking=True)
+            hout.copy_(run(i), non_blocking=True)
+        for i in range(3):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier()
+        f0 = torch.cuda.Event(enable_timing=True)
+        f1 = torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for i in range(ne):
+            e2e_step(i)
+        f1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
+
+    def e2e_pipelined_ms():
+        """The serving loop: the bound steps of two slots (device input block,
+        output), the host-to-device copies on one stream, the steps on
+        another, the device-to-host copies on a third. Step i's input copy
+        waits only for step i-2 (the last reader of its slot), so it runs
+        under step i-1's kernel, and step i's output copy under step i+1's."""
+        dins = [din, torch.empty_like(din)]
+        outs = [torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        houts = [hout, torch.empty_like(hout).pin_memory()]
+        slots = []
+        for s_ in range(2):
+            qs = dins[s_][:nq].view(B, Hq, 1, D)
+            kns = dins[s_][nq:nq + nk].view(B, Hk, 1, D)
+            vns = dins[s_][nq + nk:].view(B, Hv, 1, D)
+            row = []
+            for c in range(copies):
+                _, _, kc, vc, _, _ = caches[c]
+                if args.mode == "calibrate":
+                    row.append(ops.DecodeStep("calibrate", qs, kc, vc, threshold=thrs[c], top_n=N, out=outs[s_]))
+                else:
+                    row.append(ops.DecodeStep(args.mode, qs, kc, vc,
+                                              threshold=thrs[c] if args.mode == "atopn" else None, top_n=N,
+                                              k_new=kns, v_new=vns, append_pos=L - 1, out=outs[s_]))
+            slots.append(row)
+        comp = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_k = [torch.cuda.Event() for _ in range(2)]
+        ev_dr = [torch.cuda.Event() for _ in range(2)]
+        comp_h = comp.cuda_stream
+
+        def submit(i):
+            s_ = i & 1
+            s_in.wait_event(ev_k[s_])
+            with torch.cuda.stream(s_in):
+                dins[s_].copy_(hin, non_blocking=True)
+            ev_in[s_].record(s_in)
+            comp.wait_event(ev_in[s_])
+            comp.wait_event(ev_dr[s_])
+            slots[s_][i % copies](comp_h)
+            ev_k[s_].record(comp)
+            s_out.wait_event(ev_k[s_])
+            with torch.cuda.stream(s_out):
+                houts[s_].copy_(outs[s_], non_blocking=True)
+            ev_dr[s_].record(s_out)
+
+        def run(n):
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(comp)
+            for e in ev_k + ev_dr:  # every wait of the first steps is on work after `start`
+                e.record(comp)
+            for i in range(n):
+                submit(i)
+            for e in ev_dr:
+                comp.wait_event(e)
+            end.record(comp)
+            return start, end
+
+        run(4)
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = run(ne)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(torch, dist, f0.elapsed_time(f1) / ne, dev, world)
+
+    ms_e2e_call = e2e_ms(per_call)
+    call_api = "seqpar.ShardedDecode" if sd is not None else \
+        {"atopn": "ops.atopn_decode", "dense": "ops.dense_decode", "calibrate": "ops.atopn_calibrate"}[args.mode]
+    ms_e2e_serial = e2e_ms(lambda i: bound[i % copies]()) if bound is not None else ms_e2e_call
+    ms_e2e = e2e_pipelined_ms() if bound is not None else ms_e2e_call
 
     baselines = None
     if world == 1 and args.workload in ("config2", "config3_layer", "config5_layer") and args.mode == "atopn":
@@ -1004,7 +1102,17 @@ def main():
                 "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic", "config": config,
                 "e2e": {"value": round(job_throughput(B, ranks_b, ms_e2e), 1), "unit": unit, "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 5)},
+                        "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 5),
+                        "api": ("ops.DecodeStep, copies on two side streams overlapping the steps" if bound is not None
+                                else "seqpar.ShardedDecode")},
+                "e2e_serial": {"value": round(job_throughput(B, ranks_b, ms_e2e_serial), 1), "unit": unit,
+                               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                               "ms_per_step": round(ms_e2e_serial, 5),
+                               "api": "ops.DecodeStep" if bound is not None else call_api},
+                "e2e_per_call": {"value": round(job_throughput(B, ranks_b, ms_e2e_call), 1), "unit": unit,
+                                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                                 "ms_per_step": round(ms_e2e_call, 5),
+                                 "api": call_api},
                 "roofline": roofline, "clocks": clocks,
                 "gpu_launches": steps_timed * launches_per_step,
                 "kernels_per_step": diag["launches"], "status": status,

@@ -78,7 +78,10 @@ def _mask(attention_mask, key):
 
 def _pending(key):
     """Decode token recorded by SagaStaticCache / SagaPagedCache for this key
-    cache (or None)."""
+    cache (or None). Under torch.compile the caches copy the token themselves
+    (a graph cannot look tensors up by address), so there is none."""
+    if torch.compiler.is_compiling():
+        return None
     try:
         from .cache import take_pending
     except Exception:  # pragma: no cover - transformers missing
@@ -89,7 +92,10 @@ def _pending(key):
 def _paged(key, attention_mask):
     """For the key view of a SagaPagedCache decode step: the key and value
     pools, the mask, and the keyword arguments of the paged fused call
-    (decode token, page table, logical length); else None."""
+    (decode token, page table, logical length); else None (always under
+    torch.compile: the paged cache's address registry is eager-only)."""
+    if torch.compiler.is_compiling():
+        return None
     try:
         from .cache import take_paged
     except Exception:  # pragma: no cover - transformers missing

@@ -48,7 +48,9 @@ class SagaStaticLayer(StaticLayer):
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, *args, **kwargs):
         if not self.is_initialized:
             self.lazy_initialization(key_states, value_states)
-        if key_states.shape[-2] != 1:
+        if key_states.shape[-2] != 1 or torch.compiler.is_compiling():
+            # prefill; and decode under torch.compile, where the token is
+            # copied in the graph (the pending-token registry is eager-only)
             return super().update(key_states, value_states, *args, **kwargs)
         if self.keys.data_ptr() in _PENDING:
             raise RuntimeError("the previous decode token of this layer was never appended: "

@@ -270,6 +270,72 @@ def dense_decode(query, key, value, attention_mask=None, scaling=None, k_new=Non
     return out
 
 
+class DecodeStep:
+    """One decode op bound to fixed tensors, for serving loops.
+
+    The descriptor is built and validated once, here; every call is then a
+    single C-ABI call that reads the tensors' current contents (refill the
+    query and decode-token buffers in place, e.g. by a copy from pinned host
+    memory) and writes ``self.out``. The same kernels and arguments as
+    ``atopn_decode`` / ``atopn_calibrate`` / ``dense_decode`` with these
+    tensors. The step owns its workspace, so it never shares exchange state
+    with the per-call functions; steps must not overlap in time with each
+    other on one workspace (one stream at a time). ``op`` is "atopn",
+    "calibrate" or "dense"; ``threshold`` is read (atopn) or written
+    (calibrate).
+    """
+
+    _FN = {"atopn": ("saga_atopn_decode", L.SAGA_OP_ATOPN_DECODE),
+           "calibrate": ("saga_atopn_calibrate", L.SAGA_OP_ATOPN_CALIBRATE),
+           "dense": ("saga_dense_decode", L.SAGA_OP_DENSE_DECODE)}
+
+    def __init__(self, op: str, query, key, value, attention_mask=None, threshold=None, top_n: int = 256,
+                 scaling=None, k_new=None, v_new=None, append_pos=-1, out=None, page_table=None,
+                 context_len=None):
+        if op not in self._FN:
+            raise ValueError(f"op must be one of {sorted(self._FN)}")
+        fn_name, code = self._FN[op]
+        a = _attn_args(query, key, value, attention_mask, scaling, page_table, context_len)
+        if op != "dense":
+            if threshold is None or threshold.dtype != torch.float32 or not threshold.is_contiguous():
+                raise ValueError("threshold must be a contiguous float32 tensor with B*Hq entries")
+            if threshold.numel() < a.B * a.Hq:
+                raise ValueError("threshold has fewer than B*Hq entries")
+            a.top_n = int(top_n)
+            if op == "atopn":
+                a.thr_in = threshold.data_ptr()
+            else:
+                a.thr_out = threshold.data_ptr()
+        _set_append(a, k_new, v_new, append_pos)
+        if out is None:
+            out = _out_like(query)
+        elif out.shape != (a.B, a.Hq, 1, a.D) or out.dtype != query.dtype or out.stride(3) != 1 or not out.is_cuda:
+            raise ValueError("out must be a CUDA [B, Hq, 1, D] tensor of the query dtype, unit stride along D")
+        a.out, a.o_sb, a.o_sh = out.data_ptr(), out.stride(0), out.stride(1)
+        nbytes = L.lib.saga_workspace_bytes(ctypes.byref(a), code)
+        if nbytes == 0:
+            raise L.SagaError(L.SAGA_ERR_INVALID, "saga_workspace_bytes")
+        self.device = query.device
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        a.workspace, a.workspace_bytes = self.workspace.data_ptr(), self.workspace.numel()
+        a.status = status_tensor(self.device).data_ptr()
+        self.out = out
+        self._args = a
+        self._ref = ctypes.byref(a)
+        self._fn = getattr(L.lib, fn_name)
+        self._name = fn_name
+        # the bound tensors stay alive as long as the step
+        self._tensors = (query, key, value, attention_mask, threshold, k_new, v_new, append_pos, page_table)
+
+    def __call__(self, stream: Optional[int] = None) -> torch.Tensor:
+        """Enqueue the step on ``stream`` (a cudaStream_t as int; default:
+        the device's current torch stream) and return ``self.out``."""
+        rc = self._fn(self._ref, _stream(self.device) if stream is None else stream)
+        if rc:
+            L.check(rc, self._name)
+        return self.out
+
+
 def attn_logits(query, key, attention_mask=None, scaling=None):
     """Logits [B, Hq, 1, L] (attention.py:113-128)."""
     a = _attn_args(query, key, key[:, :1].expand(key.shape[0], 1, key.shape[2], key.shape[3]),
