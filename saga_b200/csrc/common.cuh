@@ -41,6 +41,9 @@ template <> struct Num<__nv_bfloat16> {
     uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
     return __uint_as_float(u << 16);
   }
+  // Neighbours of a positive finite bf16 value.
+  __device__ __forceinline__ static float next_up(float x) { return __uint_as_float(((__float_as_uint(x) >> 16) + 1u) << 16); }
+  __device__ __forceinline__ static float next_down(float x) { return __uint_as_float(((__float_as_uint(x) >> 16) - 1u) << 16); }
 };
 
 template <> struct Num<__half> {
@@ -57,6 +60,13 @@ template <> struct Num<__half> {
   __device__ __forceinline__ static float unkey(uint32_t k) {
     uint32_t u = (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
     return __half2float(__ushort_as_half((unsigned short)u));
+  }
+  // Neighbours of a positive finite fp16 value.
+  __device__ __forceinline__ static float next_up(float x) {
+    return __half2float(__ushort_as_half((unsigned short)(__half_as_ushort(__float2half_rn(x)) + 1u)));
+  }
+  __device__ __forceinline__ static float next_down(float x) {
+    return __half2float(__ushort_as_half((unsigned short)(__half_as_ushort(__float2half_rn(x)) - 1u)));
   }
 };
 
@@ -75,6 +85,8 @@ template <> struct Num<float> {
     uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
     return __uint_as_float(u);
   }
+  __device__ __forceinline__ static float next_up(float x) { return nextafterf(x, INFINITY); }
+  __device__ __forceinline__ static float next_down(float x) { return nextafterf(x, -INFINITY); }
 };
 
 // Load 8 consecutive elements (16 B for 16-bit types, 32 B for fp32) as floats.

@@ -58,7 +58,7 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
   const int rowb = D * esize;
   int work = tc ? ns * 128 * rowb : 2 * 64 * (rowb + 16);
   const int red = 8 * 8 * D * 4 + 8 * 8 * 4;  // per-warp values and weight sums
-  const int hist = G * 256 * 4;
+  const int hist = G * 257 * 4;  // calibration histograms, rows padded to 257 words
   // merge staging: (m, l) and scale per covered head and chunk, o per output and chunk
   const int per = (G * D + c_local - 1) / c_local;
   const int nhs = per / D + 2;

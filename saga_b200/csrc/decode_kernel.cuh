@@ -1703,16 +1703,67 @@ __device__ void merge_slice(const DecodeParams& p, int g, int jl, int b, int h0,
   trace_sub(p, 21);
 }
 
+// ---------------------------------------------------------------------------
+// Calibration over 16-bit logits with at most 16 heads per key head: a row of
+// the scores buffer is then 16 head slots, 32 bytes, read as two 16-byte
+// words, and a thread takes one position with all its heads at a time (the
+// per-head loops then run independent chains, and the reads are vectors).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void load_row16(const void* sc, int pl, uint32_t (&w)[8]) {
+  const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(sc) + (size_t)pl * 32);
+  const uint4 u0 = row[0], u1 = row[1];
+  w[0] = u0.x; w[1] = u0.y; w[2] = u0.z; w[3] = u0.w;
+  w[4] = u1.x; w[5] = u1.y; w[6] = u1.z; w[7] = u1.w;
+}
+__device__ __forceinline__ uint32_t slot16(const uint32_t (&w)[8], int h) { return (w[h >> 1] >> ((h & 1) * 16)) & 0xFFFFu; }
+// Order-preserving key of 16-bit float bits (bf16 and fp16 alike).
+__device__ __forceinline__ uint32_t key16(uint32_t raw) { return (raw & 0x8000u) ? (~raw & 0xFFFFu) : (raw | 0x8000u); }
+template <typename T>
+__device__ __forceinline__ float raw16_to_f(uint32_t raw) {
+  if constexpr (Num<T>::kDType == SAGA_BF16) return __uint_as_float(raw << 16);
+  else return __half2float(__ushort_as_half((unsigned short)raw));
+}
+// The probability of a logit rounded to the dtype (attention.py:133), out of
+// line: it is the rare path of the selection loop.
+template <typename T>
+__device__ __noinline__ float calib_prob_exact(float l, float M, float S) {
+  return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, M)), S));
+}
+
+// Warp-wide: the first key k in [lo, hi) with pred(k) true, or hi if none,
+// for a predicate that is false then true over the range. Each round the 32
+// lanes probe evenly spaced keys and the interval shrinks to the gap before
+// the first true probe: 16-bit ranges take four or five rounds.
+template <typename Pred>
+__device__ __forceinline__ uint32_t warp_first_key(uint32_t lo, uint32_t hi, Pred pred) {
+  const int lane = threadIdx.x & 31;
+  while (lo < hi) {
+    const uint32_t step = (hi - lo + 31) / 32;
+    const uint32_t pk = lo + (uint32_t)lane * step;
+    const bool valid = pk < hi;
+    const uint32_t bal = __ballot_sync(0xffffffffu, valid && pred(pk));
+    if (bal == 0u) {  // every probe false: the answer lies past the last probe
+      lo = lo + (uint32_t)((hi - lo - 1) / step) * step + 1;
+    } else {
+      const int f = __ffs(bal) - 1;
+      if (f == 0) return lo;                  // lo itself is true
+      hi = lo + (uint32_t)f * step;           // true
+      lo = lo + (uint32_t)(f - 1) * step + 1;  // past the false probe before it
+    }
+  }
+  return hi;
+}
+
 // Radix select: warp-parallel search of the bin holding the `want`-th largest
-// key among 256 bins (bin 255 = largest). Returns the bin; *above = count in
-// higher bins. Called by a full warp.
+// key among 256 bins (bin 255 = largest) of a histogram in shared memory.
+// Returns the bin; *above = count in higher bins. Called by a full warp.
 __device__ __forceinline__ int find_bin(const int* hist256, int want, int* above) {
   const int lane = threadIdx.x & 31;
   int c[8];
   int s = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    c[i] = __ldcg(&hist256[255 - lane * 8 - i]);
+    c[i] = hist256[255 - lane * 8 - i];
     s += c[i];
   }
   const int incl = warp_incl_scan(s);
@@ -2077,7 +2128,12 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       constexpr int KB = Num<T>::kKeyBits;
       constexpr int PASSES = KB / 8;
       const int nsel = p.buf_k;  // min(N, L)
-      int* hsm = reinterpret_cast<int*>(work);     // [G][256]
+      // [G][HS]: a row stride of 257 words puts the same bin of
+      // different heads in different banks (the heads' logits share their
+      // busiest bins, and neighbouring lanes hold different heads)
+      constexpr int HS = 257;
+      int* hsm = reinterpret_cast<int*>(work);
+      const bool fast16 = Num<T>::kLowp && SH == 16 && n > 0;
       // the group's histograms [pass][G][256] (shard 0's with sequence sharding)
       int* gh = p.hist_home + (size_t)g * 4 * G * 256;
       int* bctrl = SHD ? p.ctrl_home + (size_t)g * kCtrlInts : ctrl;  // barrier counters
@@ -2089,56 +2145,150 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       int sync_id = 2;
       for (int pass = 0; pass < PASSES; ++pass) {
         const int shift = KB - 8 * (pass + 1);
-        for (int i = threadIdx.x; i < G * 256; i += kThreads) hsm[i] = 0;
+        for (int i = threadIdx.x; i < G * HS; i += kThreads) hsm[i] = 0;
         __syncthreads();
-        for (int i = threadIdx.x; i < G * n; i += kThreads) {
-          const int hl = i % G, pl = i / G;
-          const uint32_t key = Num<T>::key(Num<T>::to_f(sc[pl * SH + hl]));
-          const bool match = (pass == 0) || ((key >> (shift + 8)) == (uint32_t)misc->i1[hl]);
-          if (match) atomicAdd(&hsm[hl * 256 + ((key >> shift) & 255u)], 1);
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < G * 256; i += kThreads) {
-          if (hsm[i]) {
-            if constexpr (SHD) atomicAdd_system(&gh[(size_t)pass * G * 256 + i], hsm[i]);
-            else atomicAdd(&gh[(size_t)pass * G * 256 + i], hsm[i]);
+        if (fast16) {
+          // pass 0 also sums exp(l - chunk max) per head (the fast
+          // exponential: the threshold is the sum's quotient rounded to the
+          // dtype, far coarser than its few-ulp error); the chunks' sums are
+          // rescaled to the row max after the exchange
+          uint32_t pre[16];
+          float cm[16], sacc[16];
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            pre[h] = (pass > 0 && h < G) ? (uint32_t)misc->i1[h] : 0u;
+            cm[h] = h < G ? misc->aux[h] : 0.f;
+            sacc[h] = 0.f;
+          }
+          for (int pl0 = threadIdx.x; pl0 < n; pl0 += 2 * kThreads) {
+            uint32_t w[2][8];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) load_row16(sc, min(pl0 + r * kThreads, n - 1), w[r]);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              if (pl0 + r * kThreads < n) {
+#pragma unroll
+                for (int h = 0; h < 16; ++h) {
+                  if (h < G) {
+                    const uint32_t raw = slot16(w[r], h);
+                    const uint32_t key = key16(raw);
+                    if (pass == 0 || (key >> 8) == pre[h]) atomicAdd(&hsm[h * HS + ((key >> shift) & 255u)], 1);
+                    if (pass == 0) sacc[h] += __expf(__fsub_rn(raw16_to_f<T>(raw), cm[h]));
+                  }
+                }
+              }
+            }
+          }
+          if (pass == 0) {
+            float* part = reinterpret_cast<float*>(&misc->cntw[0][0]);  // [kWarps][kMaxG]
+            const float v = warp_reduce16(sacc, [](float x, float y) { return x + y; });
+            if ((lane & 1) == 0 && (lane >> 1) < G) part[warp * kMaxG + (lane >> 1)] = v;
+            __syncthreads();
+            for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+              float v2 = 0.f;
+#pragma unroll
+              for (int k = 0; k < kWarps; ++k) v2 += part[k * kMaxG + hl];
+              st[hl].s = misc->aux[hl] == -INFINITY ? 0.f : v2;  // a fully masked chunk adds nothing
+            }
+          }
+        } else {
+          // the chunk's (position, head) pairs in the order i = pl * G + hl,
+          // walked with stride kThreads; (pl, hl) advance without a division.
+          // Neighbouring lanes hold different heads, so their atomics mostly
+          // hit different histograms.
+          const int dpl = kThreads / G, dhl = kThreads - dpl * G;
+          int pl = threadIdx.x / G, hl = threadIdx.x - (threadIdx.x / G) * G;
+          while (pl < n) {
+            const uint32_t key = Num<T>::key(Num<T>::to_f(sc[pl * SH + hl]));
+            const bool match = (pass == 0) || ((key >> (shift + 8)) == (uint32_t)misc->i1[hl]);
+            if (match) atomicAdd(&hsm[hl * HS + ((key >> shift) & 255u)], 1);
+            pl += dpl;
+            hl += dhl;
+            if (hl >= G) {
+              hl -= G;
+              ++pl;
+            }
           }
         }
-        if (pass == 1) {
+        __syncthreads();
+        trace_sub(p, pass ? 19 : 15);
+        for (int i = threadIdx.x; i < G * 256; i += kThreads) {
+          const int v = hsm[(i >> 8) * HS + (i & 255)];
+          if (v) {
+            if constexpr (SHD) atomicAdd_system(&gh[(size_t)pass * G * 256 + i], v);
+            else atomicAdd(&gh[(size_t)pass * G * 256 + i], v);
+          }
+        }
+        if (pass == 1 && !fast16) {
           // exp-sum with the global max (attention.py:131-133 softmax)
           for (int hl = warp; hl < G; hl += kWarps) {
             const float M = misc->m[hl];
             float s = 0.f;
-            for (int i = lane; i < n; i += 32) s += expf(__fsub_rn(Num<T>::to_f(sc[i * SH + hl]), M));
+            // 16-bit types: the fast exponential, since the threshold is
+            // this sum's quotient rounded to the dtype, far coarser than its
+            // few-ulp error; fp32 keeps the accurate one
+            for (int i = lane; i < n; i += 32) {
+              const float d = __fsub_rn(Num<T>::to_f(sc[i * SH + hl]), M);
+              s += Num<T>::kLowp ? __expf(d) : expf(d);
+            }
             s = warp_sum(s);
             if (lane == 0) st[hl].s = s;
           }
         }
+        trace_sub(p, pass ? 20 : 16);
         if constexpr (SHD) group_barrier_sys(&bctrl[sync_id++], C, p.status, &misc->flag);
         else group_barrier(&bctrl[sync_id++], C, true, p.status, &misc->flag);
-        if (pass == 0) {
-          for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+        trace_sub(p, pass ? 22 : 17);
+        // the chunks' statistics of a head, a lane per chunk (loads in flight
+        // together): after pass 0 the row max (and, fast path, the exp-sum
+        // with each chunk's sum rescaled from its own max); after pass 1 the
+        // exp-sum of the other path
+        if (pass == 0 || !fast16) {
+          for (int hl = warp; hl < G; hl += kWarps) {
             float M = -INFINITY;
-            for (int c = 0; c < C; ++c) M = nanmax(M, __ldcg(&stat(c, hl)->mx));
-            misc->m[hl] = M;
+            if (pass == 0) {
+              for (int c0 = 0; c0 < C; c0 += 32)
+                if (c0 + lane < C) M = nanmax(M, __ldcg(&stat(c0 + lane, hl)->mx));
+              M = warp_nanmax(M);
+            } else {
+              M = misc->m[hl];
+            }
+            float sm = 0.f;
+            if (pass == 1 || fast16) {
+              for (int c0 = 0; c0 < C; c0 += 32) {
+                if (c0 + lane < C) {
+                  const float sc_ = __ldcg(&stat(c0 + lane, hl)->s);
+                  if (pass == 1) {
+                    sm += sc_;
+                  } else {
+                    const float mc = __ldcg(&stat(c0 + lane, hl)->mx);
+                    sm += (sc_ == 0.f) ? 0.f : sc_ * __expf(mc - M);
+                  }
+                }
+              }
+              sm = warp_sum(sm);
+            }
+            if (lane == 0) {
+              if (pass == 0) misc->m[hl] = M;
+              if (pass == 1 || fast16) misc->s[hl] = sm;
+            }
           }
         }
-        if (pass == 1) {
-          for (int hl = threadIdx.x; hl < G; hl += kThreads) {
-            float s = 0.f;
-            for (int c = 0; c < C; ++c) s += __ldcg(&stat(c, hl)->s);
-            misc->s[hl] = s;
-          }
-        }
+        // the group's histograms of this pass into shared memory, all loads
+        // in flight together, then each head's bin from there
+        for (int i = threadIdx.x; i < G * 256; i += kThreads)
+          hsm[(i >> 8) * HS + (i & 255)] = __ldcg(&gh[(size_t)pass * G * 256 + i]);
+        __syncthreads();
         for (int hl = warp; hl < G; hl += kWarps) {
           int above = 0;
-          const int bin = find_bin(gh + (size_t)pass * G * 256 + hl * 256, misc->i0[hl], &above);
+          const int bin = find_bin(hsm + hl * HS, misc->i0[hl], &above);
           if (lane == 0) {
             misc->i0[hl] -= above;
             misc->i1[hl] = (int)(((uint32_t)misc->i1[hl] << 8) | (uint32_t)bin);
           }
         }
         __syncthreads();
+        trace_sub(p, pass ? 23 : 18);
       }
       // the N-th largest logit; its probability is the threshold
       // (attention.py:181-187); softmax output exp(l - M) / S rounded.
@@ -2150,15 +2300,174 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         if (jl == 0 && p.thr_out) p.thr_out[row0 + hl] = pN;  // every device's own table
       }
       __syncthreads();
-      for (int hl = warp; hl < G; hl += kWarps) {
+      // 16-bit logits, at most 16 heads and finite statistics: selection by
+      // logit thresholds (below); otherwise per position probabilities.
+      bool sel_fast = false;
+      if (fast16) {
+        int ok = 1;
+        for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+          const float M = misc->m[hl], S = misc->s[hl], pN = misc->aux[hl];
+          if (!(isfinite(M) && isfinite(S) && S > 0.f && pN >= 1e-30f && pN <= 1.f)) ok = 0;
+        }
+        sel_fast = __syncthreads_and(ok) != 0;
+      }
+      uint32_t* eqpos = list;  // per position: the heads tied at pN (the lists come later)
+      if constexpr (Num<T>::kLowp) if (sel_fast) {
+        // Per head, the smallest logits whose probability is > pN and >= pN:
+        // a warp search over the dtype's values in key order with the exact
+        // probability. The positions then compare their logits with them,
+        // two heads per instruction. The probability is non-decreasing in
+        // the logit up to expf's few-ulp error, so a position this classifies
+        // otherwise than its own probability would has a probability next to
+        // pN, a tie that the reference's own rounding could order either way.
+        for (int hl = warp; hl < 16; hl += kWarps) {
+          float tg = INFINITY, te = INFINITY;  // x > tg passes; x > te passes or ties
+          if (hl < G) {
+            const float M = misc->m[hl], S = misc->s[hl], pN = misc->aux[hl];
+            const auto pgt = [&](uint32_t k) { return calib_prob_exact<T>(Num<T>::unkey(k), M, S) > pN; };
+            const auto pge = [&](uint32_t k) { return calib_prob_exact<T>(Num<T>::unkey(k), M, S) >= pN; };
+            const uint32_t k0 = Num<T>::key(-INFINITY), k1 = Num<T>::key(INFINITY) + 1u;
+            // The N-th largest logit lN has probability pN exactly (the same
+            // expression), so the transitions sit just above and at or just
+            // below its key: one round of 32 probes on either side finds them
+            // unless many neighbouring values share pN; then the full search.
+            const uint32_t kN = Num<T>::key(misc->t[hl]);
+            uint32_t kg, ke;
+            {
+              const uint32_t pk = kN + 1u + (uint32_t)lane;
+              const uint32_t bal = __ballot_sync(0xffffffffu, pk < k1 && pgt(pk));
+              kg = bal ? kN + 1u + (uint32_t)(__ffs(bal) - 1) : warp_first_key(min(kN + 33u, k1), k1, pgt);
+            }
+            {
+              const uint32_t pk = kN - 31u + (uint32_t)lane;  // kN >= k0 >= 127: no wrap
+              const uint32_t bal = __ballot_sync(0xffffffffu, pk >= k0 && pge(pk));  // lane 31 (kN) is true
+              const int f = __ffs(bal) - 1;
+              const uint32_t p0k = kN - 31u;
+              ke = f > 0 ? p0k + (uint32_t)f : (p0k > k0 ? warp_first_key(k0, p0k, pge) : k0);
+            }
+            // prob(-inf) = 0 < pN, so kg, ke > k0 and the values below them exist
+            if (kg < k1) tg = Num<T>::unkey(kg - 1u);
+            if (ke < k1 && ke > k0) te = Num<T>::unkey(ke - 1u);
+          }
+          if (lane == 0) {
+            misc->t[hl] = tg;
+            misc->aux2[hl] = te;
+          }
+        }
+        __syncthreads();
+        trace_sub(p, 36);
+        using PT = Pair<T>;
+        using P = typename PT::P;
+        P tg2[8], te2[8];
+        uint32_t cg2[8], ce2[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          tg2[k] = PT::pack_rn(misc->t[2 * k], misc->t[2 * k + 1]);
+          te2[k] = PT::pack_rn(misc->aux2[2 * k], misc->aux2[2 * k + 1]);
+          cg2[k] = ce2[k] = 0u;
+        }
+        for (int i = threadIdx.x; i < G * (CL / 32); i += kThreads) eqb[i] = 0u;
+        __syncthreads();
+        for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
+          uint32_t gbits = 0, ebits = 0;
+          if (i < n) {
+            const uint4* row = reinterpret_cast<const uint4*>(sc + (size_t)i * 16);
+            const uint4 u0 = row[0], u1 = row[1];
+            const P* pa = reinterpret_cast<const P*>(&u0);
+            const P* pb = reinterpret_cast<const P*>(&u1);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const P v = k < 4 ? pa[k] : pb[k - 4];
+              const uint32_t gm = PT::gt_mask(v, tg2[k]) & 0x00010001u;
+              const uint32_t em = PT::gt_mask(v, te2[k]) & ~gm & 0x00010001u;
+              cg2[k] += gm;
+              ce2[k] += em;
+              gbits |= ((gm | (gm >> 15)) & 3u) << (2 * k);
+              ebits |= ((em | (em >> 15)) & 3u) << (2 * k);
+            }
+          }
+          hmask[i] = gbits;
+          eqpos[i] = ebits;
+          // the tied heads also as per-head words, for the trim below (ties
+          // are few: one shared-memory OR each)
+          while (ebits) {
+            const int hl = __ffs(ebits) - 1;
+            ebits &= ebits - 1u;
+            atomicOr(&eqb[hl * (CL / 32) + (i >> 5)], 1u << (i & 31));
+          }
+        }
+        trace_sub(p, 37);
+        trace_sub(p, 38);
+        // per-head counts: 16-bit pairs, summed over the warp, then the warps
+        int* cnt_w = reinterpret_cast<int*>(work);  // [2][kWarps][16]
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t a = (uint32_t)warp_sum_i((int)cg2[k]), e = (uint32_t)warp_sum_i((int)ce2[k]);
+          if (lane == 0) {
+            cnt_w[warp * 16 + 2 * k] = (int)(a & 0xFFFFu);
+            cnt_w[warp * 16 + 2 * k + 1] = (int)(a >> 16);
+            cnt_w[kWarps * 16 + warp * 16 + 2 * k] = (int)(e & 0xFFFFu);
+            cnt_w[kWarps * 16 + warp * 16 + 2 * k + 1] = (int)(e >> 16);
+          }
+        }
+        __syncthreads();
+        for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+          int a = 0, e = 0;
+#pragma unroll
+          for (int k = 0; k < kWarps; ++k) {
+            a += cnt_w[k * 16 + hl];
+            e += cnt_w[kWarps * 16 + k * 16 + hl];
+          }
+          st[hl].cnt = a;
+          st[hl].cnt_eq = e;
+          misc->i2[hl] = e;
+        }
+      }
+      if (!sel_fast) for (int hl = warp; hl < G; hl += kWarps) {
         const float M = misc->m[hl], S = misc->s[hl], pN = misc->aux[hl];
+        // the probability of a logit, rounded to the dtype (attention.py:133)
+        const auto prob = [&](float l) { return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, M)), S)); };
+        // 16-bit types: decide "prob > pN" and "prob == pN" from a cheap
+        // quotient __expf(l - M) / S where it is clearly away from the edges
+        // of pN's rounding interval [lo_b, hi_b], and evaluate prob() exactly
+        // near them. __expf's documented error, 2 + 1.173 |x| ulps, stays
+        // below 1.3e-5 relative wherever the quotient can reach 1e-31, ten
+        // times inside the 1e-4 margin; a tiny pN takes the exact path.
+        float lo_b = 0.f, hi_b = 0.f, invS = 0.f;
+        bool exact_all = true;
+        if constexpr (Num<T>::kLowp) {
+          exact_all = !(pN >= 1e-30f && pN <= 1.f && S > 0.f);
+          if (!exact_all) {
+            const float up = Num<T>::next_up(pN), dn = Num<T>::next_down(pN);
+            hi_b = 0.5f * (pN + up);
+            lo_b = 0.5f * (pN + dn);
+            invS = 1.f / S;
+          }
+        }
         int cg = 0, ce = 0;
         for (int w = 0; w < nw; ++w) {
           const int i = w * 32 + lane;
-          float pr = 0.f;
-          if (i < n) pr = Num<T>::round(__fdiv_rn(expf(__fsub_rn(Num<T>::to_f(sc[i * SH + hl]), M)), S));
-          const uint32_t gb = __ballot_sync(0xffffffffu, (i < n) && pr > pN);
-          const uint32_t eb = __ballot_sync(0xffffffffu, (i < n) && pr == pN);
+          bool gt = false, eq = false;
+          if (i < n) {
+            const float l = Num<T>::to_f(sc[i * SH + hl]);
+            bool exact = exact_all;
+            if (!exact) {
+              const float qf = __expf(__fsub_rn(l, M)) * invS;
+              if (qf != qf || fabsf(qf - hi_b) <= 1e-4f * hi_b || fabsf(qf - lo_b) <= 1e-4f * hi_b) {
+                exact = true;
+              } else {
+                gt = qf > hi_b;
+                eq = qf > lo_b && qf < hi_b;
+              }
+            }
+            if (exact) {
+              const float pr = prob(l);
+              gt = pr > pN;
+              eq = pr == pN;
+            }
+          }
+          const uint32_t gb = __ballot_sync(0xffffffffu, gt);
+          const uint32_t eb = __ballot_sync(0xffffffffu, eq);
           if (lane == 0) {
             sel[hl * (CL / 32) + w] = gb;
             eqb[hl * (CL / 32) + w] = eb;
@@ -2172,41 +2481,87 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
           misc->i2[hl] = ce;
         }
       }
+      trace_sub(p, 27);
       if constexpr (SHD) group_barrier_sys(&bctrl[sync_id++], C, p.status, &misc->flag);
       else group_barrier(&bctrl[sync_id++], C, true, p.status, &misc->flag);
-      // ties at the N-th probability: the lowest positions fill the set
-      for (int hl = threadIdx.x; hl < G; hl += kThreads) {
+      trace_sub(p, 28);
+      // ties at the N-th probability: the lowest positions fill the set.
+      // One warp per head, the chunks' counts loaded a lane each (all in
+      // flight together): the total above pN, then in chunk order the ties
+      // each chunk keeps, clamp(need - ties before it, 0, its ties), and the
+      // rank of this chunk's first kept position.
+      for (int hl = warp; hl < G; hl += kWarps) {
         int tot_gt = 0;
-        for (int c = 0; c < C; ++c) tot_gt += __ldcg(&stat(c, hl)->cnt);
-        const int need = max(0, nsel - tot_gt);
-        int eq_pre = 0, pos_pre = 0;
-        for (int c = 0; c < j; ++c) {
-          const int ce = __ldcg(&stat(c, hl)->cnt_eq);
-          pos_pre += __ldcg(&stat(c, hl)->cnt) + max(0, min(ce, need - eq_pre));
-          eq_pre += ce;
+        for (int c0 = 0; c0 < C; c0 += 32) {
+          const int c = c0 + lane;
+          tot_gt += c < C ? __ldcg(&stat(c, hl)->cnt) : 0;
         }
-        misc->i2[hl] = max(0, min(misc->i2[hl], need - eq_pre));  // kept ties here
-        misc->i3[hl] = max(0, pos_pre);
-        if (jl == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
+        tot_gt = warp_sum_i(tot_gt);
+        const int need = max(0, nsel - tot_gt);
+        int eq_pre = 0, pos_pre = 0;  // over the chunks before j
+        for (int c0 = 0; c0 < j; c0 += 32) {
+          const int c = c0 + lane;
+          const int ce = c < j ? __ldcg(&stat(c, hl)->cnt_eq) : 0;
+          const int cg = c < j ? __ldcg(&stat(c, hl)->cnt) : 0;
+          const int ex = eq_pre + warp_incl_scan(ce) - ce;  // ties of the chunks before c
+          pos_pre += warp_sum_i(cg + max(0, min(ce, need - ex)));
+          eq_pre += warp_sum_i(ce);
+        }
+        if (lane == 0) {
+          misc->i2[hl] = max(0, min(misc->i2[hl], need - eq_pre));  // kept ties here
+          misc->i3[hl] = max(0, pos_pre);
+          if (jl == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
+        }
       }
       __syncthreads();
+      trace_sub(p, 29);
       for (int hl = warp; hl < G; hl += kWarps) {
         warp_trim_bits(eqb + hl * (CL / 32), nw, misc->i2[hl]);
-        for (int w = lane; w < nw; w += 32) sel[hl * (CL / 32) + w] |= eqb[hl * (CL / 32) + w];
-        __syncwarp();
-        if (p.sel_idx_out && misc->i3[hl] < p.sel_ld)
-          warp_write_positions(sel + hl * (CL / 32), nw, p.pos_offset + p0,
-                               p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
-                               max(0, p.sel_ld - misc->i3[hl]));
+        if (!sel_fast) {
+          for (int w = lane; w < nw; w += 32) sel[hl * (CL / 32) + w] |= eqb[hl * (CL / 32) + w];
+          __syncwarp();
+          if (p.sel_idx_out && misc->i3[hl] < p.sel_ld)
+            warp_write_positions(sel + hl * (CL / 32), nw, p.pos_offset + p0,
+                                 p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
+                                 max(0, p.sel_ld - misc->i3[hl]));
+        }
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
-        uint32_t bits = 0;
-        if (i < n)
-          for (int hl = 0; hl < G; ++hl) bits |= ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) << hl;
-        hmask[i] = bits;
+      trace_sub(p, 30);
+      if (sel_fast) {
+        // the kept ties join the passing heads of their positions
+        for (int w = warp; w < nw; w += kWarps) {
+          const int i = w * 32 + lane;
+          if (__ballot_sync(0xffffffffu, eqpos[i] != 0u)) {
+            uint32_t add = 0;
+            for (int hl = 0; hl < G; ++hl) add |= ((eqb[hl * (CL / 32) + w] >> lane) & 1u) << hl;
+            hmask[i] |= add;
+          }
+        }
+        if (p.sel_idx_out) {  // diagnostics: the kept positions from the final masks
+          __syncthreads();
+          for (int hl = warp; hl < G; hl += kWarps) {
+            for (int w = 0; w < nw; ++w) {
+              const uint32_t bb = __ballot_sync(0xffffffffu, (hmask[w * 32 + lane] >> hl) & 1u);
+              if (lane == 0) sel[hl * (CL / 32) + w] = bb;
+            }
+            __syncwarp();
+            if (misc->i3[hl] < p.sel_ld)
+              warp_write_positions(sel + hl * (CL / 32), nw, p.pos_offset + p0,
+                                   p.sel_idx_out + (size_t)(row0 + hl) * p.sel_ld + misc->i3[hl],
+                                   max(0, p.sel_ld - misc->i3[hl]));
+          }
+        }
+      } else {
+        for (int i = threadIdx.x; i < nw * 32; i += kThreads) {
+          uint32_t bits = 0;
+          if (i < n)
+            for (int hl = 0; hl < G; ++hl) bits |= ((sel[hl * (CL / 32) + (i >> 5)] >> (i & 31)) & 1u) << hl;
+          hmask[i] = bits;
+        }
       }
       __syncthreads();
+      trace_sub(p, 34);
       gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
       if constexpr (kTcPv)
         gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
