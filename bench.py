@@ -391,6 +391,48 @@ def gpu_baselines(torch, ops, shape, dev, caches, steps: int):
             out["reference_atopn_us"] = round(1e3 * graph_ms(torch, stream, fns, steps), 3)
         except Exception as e:  # the reference's GPU path is a reported baseline only
             out["reference_atopn_error"] = f"{type(e).__name__}: {e}"[:300]
+    # the calibration step (first decode step of a generation) on the same
+    # caches, with its algorithmic bytes: the key cache, and the value rows of
+    # the union of the top-N sets of the heads sharing a value head
+    copies = len(caches)
+    thr_c = [torch.zeros(B * Hq, dtype=torch.float32, device=dev) for _ in range(copies)]
+    d = {}
+    ops.atopn_calibrate(caches[0][1], caches[0][2], caches[0][3], None, thr_c[0], N, diag=d)
+    torch.cuda.synchronize()
+    sel = d["sel_idx"].cpu()
+    Gv = Hq // Hv
+    union = 0
+    for b in range(B):
+        for vh in range(Hv):
+            rows = set()
+            for h in range(vh * Gv, (vh + 1) * Gv):
+                rows.update(sel[b * Hq + h, :N].tolist())
+            rows.discard(-1)
+            union += len(rows)
+    with torch.cuda.stream(stream):
+        fns = [(lambda c=c: ops.atopn_calibrate(caches[c][1], caches[c][2], caches[c][3], None, thr_c[c], N))
+               for c in range(copies)]
+        for f in fns:
+            f()
+    cal_ms = graph_ms(torch, stream, fns, steps)
+    cal_bytes = B * Hk * L * D * 2 + union * D * 2
+    peak, peak_kind = measured_peaks()
+    out["calibrate_us"] = round(1e3 * cal_ms, 3)
+    out["calibrate_roofline"] = {"bound": "hbm", "achieved": round(cal_bytes / (cal_ms * 1e-3) / 1e9, 1), "peak": peak,
+                                 "unit": "GB/s", "frac": round(cal_bytes / (cal_ms * 1e-3) / 1e9 / peak, 4),
+                                 "peak_kind": peak_kind, "algorithmic_bytes_per_step": cal_bytes,
+                                 "value_rows_union_per_step": union}
+    if A is not None:
+        try:
+            with torch.cuda.stream(stream):
+                fns = [(lambda c=c: A.approx_top_n_attention_amortized_cal(caches[c][1], caches[c][2], caches[c][3], None,
+                                                                          top_n_attention=N, layer_idx=c))
+                       for c in range(copies)]
+                for f in fns:
+                    f()
+            out["reference_calibrate_us"] = round(1e3 * graph_ms(torch, stream, fns, steps), 3)
+        except Exception as e:
+            out["reference_calibrate_error"] = f"{type(e).__name__}: {e}"[:300]
     # dense GQA of the unmerged model (the reference's baseline, eval.md:60-65)
     gshape = (B, L, Hq, Hv, Hv, D, N, 0)
     gq = [make_device_inputs(torch, gshape, dev, seed=100 + c) for c in range(2)]
