@@ -181,12 +181,35 @@ static int compute_decode_plan(const SagaAttnArgs* a, int mode, DecodePlan* pl, 
     c_par = std::max(1, di.sms / std::max(1, groups));
   }
   if (tc) {
+    bool one_wave = false;
     for (int s = kMaxStages; s >= 2; --s) {
       const int mt = tiles_for(s);
       if (mt > 0 && (ntiles + mt - 1) / mt <= c_par) {
         ns = s;
         max_tiles = mt;
+        one_wave = true;
         break;
+      }
+    }
+    if (!one_wave) {
+      // The items run in rounds of one per SM. Ring depth and chunk length
+      // with the fewest rounds x (tiles per chunk + about six tiles' worth of
+      // per-item exchanges and merge); deeper rings win ties. E.g. dense
+      // decode with unmerged key heads at config 2: 18 chunks of 15 tiles per
+      // group on a 3-stage ring run in 2 rounds, not 20 of 13 in 3.
+      long best = -1;
+      for (int s = kMaxStages; s >= 2; --s) {
+        const int mt = tiles_for(s);
+        for (int t = mt; t >= 1; --t) {
+          const long cc = (ntiles + t - 1) / t;
+          const long rounds = ((long)groups * cc + target - 1) / target;
+          const long cost = rounds * (t + 6);
+          if (best < 0 || cost < best) {
+            best = cost;
+            ns = s;
+            max_tiles = t;
+          }
+        }
       }
     }
   }
@@ -354,46 +377,53 @@ int launch_decode(const SagaAttnArgs* a, int mode, cudaStream_t stream, std::str
       return SAGA_ERR_CUDA;
     }
     const uint64_t es = 2;
-    // strides of size-1 dims do not matter; keep them valid (multiples of 16 B)
-    // contiguous: {D, L, Hk, B}; paged: {D, page_len, Hk, num_pages} over the pool
     const bool paged = a->page_table != nullptr;
-    const uint64_t rows = paged ? (uint64_t)a->page_len : (uint64_t)a->L;
-    const uint64_t outer = paged ? (uint64_t)a->num_pages : (uint64_t)a->B;
-    const uint64_t sl = (uint64_t)a->k_sl * es;
-    const uint64_t sh = a->Hk > 1 ? (uint64_t)a->k_sh * es : sl * rows;
-    const uint64_t sb = outer > 1 ? (uint64_t)a->k_sb * es : sh * (uint64_t)a->Hk;
-    cuuint64_t dims[4] = {(cuuint64_t)a->D, (cuuint64_t)rows, (cuuint64_t)a->Hk, (cuuint64_t)outer};
-    cuuint64_t strides[3] = {sl, sh, sb};
-    cuuint32_t box[4] = {64, 128, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    // the map depends only on the cache's address, dtype, extents and strides:
-    // the last few are kept (a decode loop cycles over one cache per layer)
-    const std::array<unsigned long long, 9> tkey = {(unsigned long long)reinterpret_cast<uintptr_t>(a->k),
-                                                    (unsigned long long)a->dtype, dims[0], dims[1], dims[2], dims[3],
-                                                    sl, sh, sb};
-    static std::mutex tmu;
-    static std::map<std::array<unsigned long long, 9>, CUtensorMap> tmaps;
-    bool have = false;
-    {
-      std::lock_guard<std::mutex> lock(tmu);
-      auto it = tmaps.find(tkey);
-      if (it != tmaps.end()) {
-        p.tmap = it->second;
-        have = true;
+    // strides of size-1 dims do not matter; keep them valid (multiples of 16 B)
+    // contiguous: {D, L, H, B}; paged: {D, page_len, H, num_pages} over the pool
+    auto encode = [&](CUtensorMap* out, const void* base, int H, int64_t s_l, int64_t s_h, int64_t s_b,
+                      const char* what) -> int {
+      const uint64_t rows = paged ? (uint64_t)a->page_len : (uint64_t)a->L;
+      const uint64_t outer = paged ? (uint64_t)a->num_pages : (uint64_t)a->B;
+      const uint64_t sl = (uint64_t)s_l * es;
+      const uint64_t sh = H > 1 ? (uint64_t)s_h * es : sl * rows;
+      const uint64_t sb = outer > 1 ? (uint64_t)s_b * es : sh * (uint64_t)H;
+      cuuint64_t dims[4] = {(cuuint64_t)a->D, (cuuint64_t)rows, (cuuint64_t)H, (cuuint64_t)outer};
+      cuuint64_t strides[3] = {sl, sh, sb};
+      cuuint32_t box[4] = {64, 128, 1, 1};
+      cuuint32_t estr[4] = {1, 1, 1, 1};
+      // the map depends only on the cache's address, dtype, extents and strides:
+      // the last few are kept (a decode loop cycles over one cache per layer)
+      const std::array<unsigned long long, 9> tkey = {(unsigned long long)reinterpret_cast<uintptr_t>(base),
+                                                      (unsigned long long)a->dtype, dims[0], dims[1], dims[2], dims[3],
+                                                      sl, sh, sb};
+      static std::mutex tmu;
+      static std::map<std::array<unsigned long long, 9>, CUtensorMap> tmaps;
+      {
+        std::lock_guard<std::mutex> lock(tmu);
+        auto it = tmaps.find(tkey);
+        if (it != tmaps.end()) {
+          *out = it->second;
+          return SAGA_OK;
+        }
       }
-    }
-    if (!have) {
-      CUresult r = enc(&p.tmap,
-                       a->dtype == SAGA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                       const_cast<void*>(a->k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      CUresult r = enc(out, a->dtype == SAGA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                       4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       if (r != CUDA_SUCCESS) {
-        *err = "cuTensorMapEncodeTiled failed for the key cache (" + std::to_string((int)r) + ")";
+        *err = std::string("cuTensorMapEncodeTiled failed for the ") + what + " (" + std::to_string((int)r) + ")";
         return SAGA_ERR_INVALID;
       }
       std::lock_guard<std::mutex> lock(tmu);
       if (tmaps.size() >= 256) tmaps.clear();
-      tmaps[tkey] = p.tmap;
+      tmaps[tkey] = *out;
+      return SAGA_OK;
+    };
+    int rc = encode(&p.tmap, a->k, a->Hk, a->k_sl, a->k_sh, a->k_sb, "key cache");
+    if (rc != SAGA_OK) return rc;
+    // dense steps on the tensor-core P.V stream the value tiles by TMA as well
+    if (mode == MODE_DENSE && a->D == 128 && !paged) {
+      rc = encode(&p.vmap, a->v, a->Hv, a->v_sl, a->v_sh, a->v_sb, "value cache");
+      if (rc != SAGA_OK) return rc;
     }
   }
 

@@ -105,6 +105,7 @@ __host__ __device__ inline SmemLayout smem_layout(int G, int D, int CL, int esiz
 
 struct DecodeParams {
   CUtensorMap tmap;  // key cache, 4-D {D, L, Hk, B}, 64 x 128 boxes, 128-B swizzle (tensor-core path)
+  CUtensorMap vmap;  // value cache, the same form over {D, L, Hv, B} (dense mode, tensor-core P.V)
   int B, Hq, Hk, Hv, D, L, G, Gv;
   int C, CL, items, tail, buf_k, ns, nvh, sh;
   int tmem_cols;  // TMEM columns per CTA: the scorer's kScoreBufs x 16, or up to 4 x 16 per gather group for the P.V

@@ -86,6 +86,8 @@ struct Misc {
   int gpad[kMaxGatherGroups + 1];    // tensor-core P.V: first row slot of each gather group (16-aligned)
   float lacc[16 * 8];                // tensor-core P.V: weight sums per (gather group, head)
   uint64_t pvbar;                    // tensor-core P.V: a pass's MMAs completed
+  uint64_t wfull[kMaxStages];        // dense P.V: a ring stage's weights written (4 epilogue warps)
+  uint32_t vs0, vph0;                // dense P.V: ring stage and phase of its first value tile
   int ngroups;
   int flag;
   int last;
@@ -153,6 +155,7 @@ struct Ring {
   uint32_t ms = 0, mph = 0;   // UMMA issuer stage / phase
   uint32_t mb = 0, mbph = 0;  // UMMA issuer TMEM buffer / phase
   uint32_t eb = 0, ebph = 0;  // epilogue TMEM buffer / phase
+  uint32_t wpar = 0;          // UMMA issuer: next parity of each stage's wfull barrier (dense P.V)
 };
 
 // Optional phase trace (diagnostics), compiled in only when the library is
@@ -1483,6 +1486,192 @@ __device__ void gather_end_tc(const DecodeParams& p, int g, int j, int b, int p0
   if (tr) trace_stamp(p, 14);
 }
 
+// ---------------------------------------------------------------------------
+// Dense P.V with the value rows streamed by TMA (16-bit types, head_dim 128,
+// contiguous caches; attention.py:64-85). The chunk's value rows of each
+// gather group's value head flow through the key ring in 128-row tiles: two
+// 64-column boxes with the 128-B swizzle are the MN-major A operand as TMA
+// lays them out (8-row atoms 1024 B apart, the second half of head_dim 16 KB
+// on). The 4 epilogue warps write each tile's weights exp(l - chunk max),
+// rounded to the value type, as the K-major B operand of that ring stage
+// (16 head slots, the group's heads and zeros), keep the sums of the rounded
+// weights, and arrive on the stage's wfull barrier; warp 0 refills stages
+// once their MMAs are done, and one elected thread of warp 1 issues the MMAs
+// (M = 128 head_dim rows, N = 16 head slots, K = 16 positions) into the
+// group's round-robin TMEM accumulators. The ring state carries on from the
+// scorer, so the stages and their barriers serve both phases.
+// ---------------------------------------------------------------------------
+template <typename T, int D, bool SHD>
+__device__ void dense_stream_pv(const DecodeParams& p, int g, int j, int b, int p0, int n,
+                                const T* __restrict__ sc, uint8_t* __restrict__ ring, uint8_t* __restrict__ wpv,
+                                float* __restrict__ part, Misc* misc, Ring& rg, uint32_t tmem_base, uint32_t& pvph) {
+  static_assert(D == 128, "the streamed P.V covers head_dim 128");
+  constexpr uint32_t TILE_BYTES = 128u * D * 2u;
+  constexpr uint32_t W_BYTES = 4096u;  // weights of one tile: 2 blocks of 64 positions x 16 head slots
+  constexpr uint32_t kIdesc = umma_idesc_f16(Num<T>::kDType == SAGA_BF16 ? 1u : 0u, 128, 16) | kUmmaAMajorMN;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int NS = p.ns, SH = p.sh, G = p.G;
+  const int ngroups = misc->ngroups;
+  const int ntl = (n + 127) / 128;
+  const int nsteps = ngroups * ntl;
+  const int nch = min(4, p.tmem_cols / (16 * max(ngroups, 1)));
+  const uint32_t tag = misc->tag;
+  if (warp == 1 && lane == 0) {
+    misc->vs0 = rg.ms;
+    misc->vph0 = rg.mph;
+  }
+  __syncthreads();
+  const uint32_t vs0 = misc->vs0, vph0 = misc->vph0;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < nsteps && !misc->abort; ++k) {
+        if (!mbar_wait(&misc->empty[rg.ps], rg.pph ^ 1u, p.status)) {
+          misc->abort = 1;
+          break;
+        }
+        const int gi = k / ntl, t = k - gi * ntl;
+        mbar_arrive_expect_tx(&misc->full[rg.ps], TILE_BYTES);
+        uint8_t* dst = ring + rg.ps * TILE_BYTES;
+#pragma unroll
+        for (int kb = 0; kb < D / 64; ++kb)
+          tma_load_4d(dst + kb * 16384, &p.vmap, kb * 64, p0 + t * 128, misc->gvh[gi], b, &misc->full[rg.ps]);
+        ++issued;
+        if (++rg.ps == (uint32_t)NS) {
+          rg.ps = 0;
+          rg.pph ^= 1u;
+        }
+      }
+      if (misc->abort) {  // drain: the last issued tiles may still be landing
+        uint32_t s2 = rg.ps, ph = rg.pph;
+        for (int k = 0; k < min(issued, NS); ++k) {
+          if (s2 == 0) {
+            s2 = NS - 1;
+            ph ^= 1u;
+          } else {
+            --s2;
+          }
+          mbar_wait(&misc->full[s2], ph, p.status);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int ks = 0;  // K steps of the current group
+      for (int k = 0; k < nsteps && !misc->abort; ++k) {
+        const int gi = k / ntl, t = k - gi * ntl;
+        if (t == 0) ks = 0;
+        if (!mbar_wait(&misc->full[rg.ms], rg.mph, p.status) ||
+            !mbar_wait(&misc->wfull[rg.ms], (rg.wpar >> rg.ms) & 1u, p.status)) {
+          misc->abort = 1;
+          break;
+        }
+        rg.wpar ^= 1u << rg.ms;
+        tc_fence_after();
+        const uint64_t ad0 = umma_desc_mn_sw128(smem_addr(ring + rg.ms * TILE_BYTES), 16384, 1024);
+        const uint64_t bd0 = umma_desc_sw128(smem_addr(wpv + rg.ms * W_BYTES));
+        const int rows = min(128, n - t * 128);
+        for (int ps = 0; ps < rows; ps += 16, ++ks) {
+          // start addresses in 16-byte units: 16 rows are 2048 B of A; 32 B of
+          // weights within a 64-position block, 2048 B per block
+          const uint64_t ad = ad0 + (uint64_t)(ps * 8);
+          const uint64_t bd = bd0 + (uint64_t)((ps >> 6) * 128 + ((ps & 63) >> 4) * 2);
+          const int c = ks % nch;
+          umma_f16(tmem_base + (uint32_t)(gi * nch + c) * 16u, ad, bd, kIdesc, ks < nch ? 0u : 1u);
+        }
+        umma_commit(&misc->empty[rg.ms]);
+        if (++rg.ms == (uint32_t)NS) {
+          rg.ms = 0;
+          rg.mph ^= 1u;
+        }
+      }
+      umma_commit(&misc->pvbar);  // every MMA of the item, also after an abort
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int tid = threadIdx.x - 128;  // position within a tile
+    float ls[8];
+#pragma unroll
+    for (int hh = 0; hh < 8; ++hh) ls[hh] = 0.f;
+    for (int k = 0; k < nsteps; ++k) {
+      const int gi = k / ntl, t = k - gi * ntl;
+      const uint32_t u = vs0 + (uint32_t)k;
+      const uint32_t s2 = u % (uint32_t)NS;
+      const uint32_t ph = vph0 ^ ((u / (uint32_t)NS) & 1u);
+      // the stage's previous MMAs (they read its weights) are complete
+      if (!mbar_wait(&misc->empty[s2], ph ^ 1u, p.status)) {
+        misc->abort = 1;
+        break;
+      }
+      const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+      const int pos = t * 128 + tid;
+      uint8_t* wb = wpv + s2 * W_BYTES;
+#pragma unroll
+      for (int hh = 0; hh < 16; ++hh) {
+        T e = Num<T>::from_f(0.f);
+        if (hh < nh && pos < n)
+          e = Num<T>::from_f(__expf(Num<T>::to_f(sc[pos * SH + hb + hh]) - misc->aux[hb + hh]));
+        *reinterpret_cast<T*>(wb + pv_w_off(tid, hh)) = e;
+        if (hh < 8) ls[hh] += Num<T>::to_f(e);  // the rounded weight the MMA multiplies
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&misc->wfull[s2]);
+      if (t == ntl - 1) {  // the group's weight sums: per warp, in a fixed order
+#pragma unroll
+        for (int hh = 0; hh < 8; ++hh) {
+          const float v = warp_sum(ls[hh]);
+          if (lane == 0) part[((warp - 4) * ngroups + gi) * 8 + hh] = v;
+          ls[hh] = 0.f;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  trace_stamp(p, 12);
+  mbar_wait(&misc->pvbar, pvph, p.status);
+  pvph ^= 1u;
+  tc_fence_after();
+  trace_stamp(p, 13);
+  for (int t2 = threadIdx.x; t2 < ngroups * 8; t2 += kThreads) {
+    const int gi = t2 >> 3, hh = t2 & 7;
+    misc->lacc[t2] = ((part[(0 * ngroups + gi) * 8 + hh] + part[(1 * ngroups + gi) * 8 + hh]) +
+                      part[(2 * ngroups + gi) * 8 + hh]) + part[(3 * ngroups + gi) * 8 + hh];
+  }
+  // accumulators -> slots: warp w reads TMEM lanes 32 (w % 4) .. + 31 (d),
+  // warps 0-3 the even gather groups, 4-7 the odd ones
+  {
+    const int q = warp & 3;
+    const int d = q * 32 + lane;
+    const int used = min(nch, (n + 15) / 16);  // accumulators that received a K step
+    for (int gi = warp >> 2; gi < ngroups && warp < 8; gi += 2) {
+      const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+      float o[8];
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh) o[hh] = 0.f;
+      for (int c = 0; c < used; ++c) {  // fixed order: run-to-run identical sums
+        uint32_t r[16];
+        tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((gi * nch + c) * 16), r);
+#pragma unroll
+        for (int hh = 0; hh < 8; ++hh) o[hh] += __uint_as_float(r[hh]);
+      }
+#pragma unroll
+      for (int hh = 0; hh < 8; ++hh)
+        if (hh < nh) slot_put<SHD>(slot_at<SHD>(p, g, j, hb + hh, kSlotO + d), tag, __float_as_uint(o[hh]));
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  for (int t2 = threadIdx.x; t2 < ngroups * 8; t2 += kThreads) {
+    const int gi = t2 >> 3, hh = t2 & 7;
+    if (hh < (misc->ghb[gi] >> 16))
+      slot_put<SHD>(slot_at<SHD>(p, g, j, (misc->ghb[gi] & 0xFFFF) + hh, kSlotL), tag, __float_as_uint(misc->lacc[t2]));
+  }
+  for (int hl = threadIdx.x; hl < G; hl += kThreads)
+    slot_put<SHD>(slot_at<SHD>(p, g, j, hl, kSlotM), tag, __float_as_uint(misc->aux[hl]));
+  trace_stamp(p, 14);
+}
+
 template <typename T, int D, int MODE, bool SHD, bool PG>
 __device__ void gather_end(const DecodeParams& p, int g, int j, int b, int h0, int p0, int n,
                            const T* __restrict__ sc, const uint32_t* __restrict__ hmask,
@@ -1834,6 +2023,7 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       mbar_init(&misc->tempty[bb], 4);
     }
     mbar_init(&misc->pvbar, 1);
+    for (int s = 0; s < kMaxStages; ++s) mbar_init(&misc->wfull[s], 4);
     misc->abort = 0;
     mbar_fence_init();
   }
@@ -2568,11 +2758,23 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       else
         gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
     } else {  // MODE_DENSE: misc->aux holds the chunk max from the scoring pass
-      gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
-      if constexpr (kTcPv)
-        gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
-      else
-        gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+      bool streamed = false;
+      if constexpr (kTcPv && !PG) {
+        // value tiles by TMA when the weight buffer holds one tile per ring
+        // stage (the layout gives it that for every ring depth it plans)
+        if (p.sm.brw >= p.ns * 64) {
+          dense_stream_pv<T, D, SHD>(p, g, j, b, p0, n, sc, work, wpv, reinterpret_cast<float*>(list), misc, rg,
+                                     tmem_base, pvph);
+          streamed = true;
+        }
+      }
+      if (!streamed) {
+        gather_begin<T, D, MODE, kTcPv, PG>(p, b, p0, n, sc, hmask, list, toff, occ, work, wpv, misc);
+        if constexpr (kTcPv)
+          gather_end_tc<T, D, MODE, SHD, PG>(p, g, j, b, p0, sc, hmask, list, work, wpv, misc, tmem_base, pvph, false);
+        else
+          gather_end<T, D, MODE, SHD, PG>(p, g, j, b, h0, p0, n, sc, hmask, list, work, wbuf, misc);
+      }
     }
     __syncthreads();
 
