@@ -1558,10 +1558,10 @@ __device__ void dense_stream_pv(const DecodeParams& p, int g, int j, int b, int 
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      int ks = 0;  // K steps of the current group
+      int ks = 0, acc_c = 0;  // K steps of the current group; its next accumulator
       for (int k = 0; k < nsteps && !misc->abort; ++k) {
         const int gi = k / ntl, t = k - gi * ntl;
-        if (t == 0) ks = 0;
+        if (t == 0) ks = acc_c = 0;
         if (!mbar_wait(&misc->full[rg.ms], rg.mph, p.status) ||
             !mbar_wait(&misc->wfull[rg.ms], (rg.wpar >> rg.ms) & 1u, p.status)) {
           misc->abort = 1;
@@ -1571,14 +1571,21 @@ __device__ void dense_stream_pv(const DecodeParams& p, int g, int j, int b, int 
         tc_fence_after();
         const uint64_t ad0 = umma_desc_mn_sw128(smem_addr(ring + rg.ms * TILE_BYTES), 16384, 1024);
         const uint64_t bd0 = umma_desc_sw128(smem_addr(wpv + rg.ms * W_BYTES));
-        const int rows = min(128, n - t * 128);
-        for (int ps = 0; ps < rows; ps += 16, ++ks) {
-          // start addresses in 16-byte units: 16 rows are 2048 B of A; 32 B of
-          // weights within a 64-position block, 2048 B per block
-          const uint64_t ad = ad0 + (uint64_t)(ps * 8);
-          const uint64_t bd = bd0 + (uint64_t)((ps >> 6) * 128 + ((ps & 63) >> 4) * 2);
-          const int c = ks % nch;
-          umma_f16(tmem_base + (uint32_t)(gi * nch + c) * 16u, ad, bd, kIdesc, ks < nch ? 0u : 1u);
+        const int steps = min(8, (n - t * 128 + 15) >> 4);  // 16-row K steps with real rows
+        // The issuing warp shares its scheduler with a weight-building warp,
+        // so the loop is kept to a few instructions per MMA: descriptors by
+        // constant offsets (16-byte units: 16 rows are 2048 B of A; 32 B of
+        // weights within a 64-position block, 2048 B per block), the
+        // accumulator by a wrapping counter.
+        const uint32_t tg = tmem_base + (uint32_t)(gi * nch) * 16u;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q < steps) {
+            umma_f16(tg + (uint32_t)acc_c * 16u, ad0 + (uint64_t)(q * 128),
+                     bd0 + (uint64_t)((q >> 2) * 128 + (q & 3) * 2), kIdesc, ks < nch ? 0u : 1u);
+            ++ks;
+            acc_c = (acc_c + 1 == nch) ? 0 : acc_c + 1;
+          }
         }
         umma_commit(&misc->empty[rg.ms]);
         if (++rg.ms == (uint32_t)NS) {
