@@ -584,11 +584,15 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
         const uint32_t a0 = smem_addr(ring + rg.ms * TILE_BYTES);
         const uint32_t b0 = smem_addr(qop);
         const uint32_t dt = tmem_base + rg.mb * 16u;
+        // descriptors of the tile's first K step, then constant offsets (the
+        // start-address field counts 16-byte units): this warp shares its
+        // scheduler with an epilogue warp, so few instructions per MMA
+        const uint64_t ad0 = umma_desc_sw128(a0), bd0 = umma_desc_sw128(b0);
 #pragma unroll
         for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(dt, umma_desc_sw128(a0 + kb * 16384 + kk * 32), umma_desc_sw128(b0 + kb * 2048 + kk * 32),
+            umma_f16(dt, ad0 + (uint64_t)((kb * 16384 + kk * 32) >> 4), bd0 + (uint64_t)((kb * 2048 + kk * 32) >> 4),
                      IDESC, (kb | kk) != 0);
         umma_commit(&misc->empty[rg.ms]);
         umma_commit(&misc->tfull[rg.mb]);
