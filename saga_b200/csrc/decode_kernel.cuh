@@ -2361,20 +2361,38 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
             cm[h] = h < G ? misc->aux[h] : 0.f;
             sacc[h] = 0.f;
           }
-          for (int pl0 = threadIdx.x; pl0 < n; pl0 += 2 * kThreads) {
-            uint32_t w[2][8];
+          // the two passes as separate loops, each with only its own work
+          if (pass == 0) {
+            for (int pl0 = threadIdx.x; pl0 < n; pl0 += 2 * kThreads) {
+              uint32_t w[2][8];
 #pragma unroll
-            for (int r = 0; r < 2; ++r) load_row16(sc, min(pl0 + r * kThreads, n - 1), w[r]);
+              for (int r = 0; r < 2; ++r) load_row16(sc, min(pl0 + r * kThreads, n - 1), w[r]);
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-              if (pl0 + r * kThreads < n) {
+              for (int r = 0; r < 2; ++r) {
+                if (pl0 + r * kThreads < n) {
 #pragma unroll
-                for (int h = 0; h < 16; ++h) {
-                  if (h < G) {
-                    const uint32_t raw = slot16(w[r], h);
-                    const uint32_t key = key16(raw);
-                    if (pass == 0 || (key >> 8) == pre[h]) atomicAdd(&hsm[h * HS + ((key >> shift) & 255u)], 1);
-                    if (pass == 0) sacc[h] += __expf(__fsub_rn(raw16_to_f<T>(raw), cm[h]));
+                  for (int h = 0; h < 16; ++h) {
+                    if (h < G) {
+                      const uint32_t raw = slot16(w[r], h);
+                      atomicAdd(&hsm[h * HS + (key16(raw) >> 8)], 1);
+                      sacc[h] += __expf(__fsub_rn(raw16_to_f<T>(raw), cm[h]));
+                    }
+                  }
+                }
+              }
+            }
+          } else {
+            for (int pl0 = threadIdx.x; pl0 < n; pl0 += 2 * kThreads) {
+              uint32_t w[2][8];
+#pragma unroll
+              for (int r = 0; r < 2; ++r) load_row16(sc, min(pl0 + r * kThreads, n - 1), w[r]);
+#pragma unroll
+              for (int r = 0; r < 2; ++r) {
+                if (pl0 + r * kThreads < n) {
+#pragma unroll
+                  for (int h = 0; h < 16; ++h) {
+                    const uint32_t key = key16(slot16(w[r], h));
+                    if (h < G && (key >> 8) == pre[h]) atomicAdd(&hsm[h * HS + (key & 255u)], 1);
                   }
                 }
               }
