@@ -28,8 +28,9 @@ baseline/install_reference.sh, with its Triton selection replaced by a torch
 compaction), the whole batch per step, with all torch threads; it falls back to
 the numpy port of its algorithm (oracle/) when the reference is not installed.
 The default line also reports, on the GPU, the reference's own torch + Triton
-step and dense GQA decode (this library's kernel and the reference's torch
-bmm) under "gpu_baselines".
+step and calibration, this library's calibration step with its roofline, and
+dense GQA decode (this library's kernel and the reference's torch bmm) under
+"gpu_baselines".
 """
 from __future__ import annotations
 
