@@ -2462,7 +2462,66 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
         // together): after pass 0 the row max (and, fast path, the exp-sum
         // with each chunk's sum rescaled from its own max); after pass 1 the
         // exp-sum of the other path
-        if (pass == 0 || !fast16) {
+        // the group's histograms of this pass, loaded into registers first so
+        // that every load is in flight at once (stored below)
+        int hv[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int i = threadIdx.x + k * kThreads;
+          hv[k] = i < G * 256 ? __ldcg(&gh[(size_t)pass * G * 256 + i]) : 0;
+        }
+        if ((pass == 0 || !fast16) && C <= 32) {
+          // a lane per chunk, both of a warp's heads at once: one round of loads
+          const int h0w = warp, h1w = warp + kWarps;
+          const bool has0 = h0w < G, has1 = h1w < G;
+          const bool on = lane < C;
+          float mx0 = -INFINITY, mx1 = -INFINITY, s0 = 0.f, s1 = 0.f;
+          if (on && has0) {
+            mx0 = __ldcg(&stat(lane, h0w)->mx);
+            s0 = __ldcg(&stat(lane, h0w)->s);
+          }
+          if (on && has1) {
+            mx1 = __ldcg(&stat(lane, h1w)->mx);
+            s1 = __ldcg(&stat(lane, h1w)->s);
+          }
+          float M0 = pass == 0 ? warp_nanmax(mx0) : (has0 ? misc->m[h0w] : 0.f);
+          float M1 = pass == 0 ? warp_nanmax(mx1) : (has1 ? misc->m[h1w] : 0.f);
+          float a0 = 0.f, a1 = 0.f;
+          if (pass == 1) {
+            a0 = s0;
+            a1 = s1;
+          } else if (fast16) {
+            a0 = (s0 == 0.f) ? 0.f : s0 * __expf(mx0 - M0);
+            a1 = (s1 == 0.f) ? 0.f : s1 * __expf(mx1 - M1);
+          }
+          a0 = warp_sum(a0);
+          a1 = warp_sum(a1);
+          if (lane == 0) {
+            if (has0) {
+              if (pass == 0) misc->m[h0w] = M0;
+              if (pass == 1 || fast16) misc->s[h0w] = a0;
+            }
+            if (has1) {
+              if (pass == 0) misc->m[h1w] = M1;
+              if (pass == 1 || fast16) misc->s[h1w] = a1;
+            }
+          }
+          for (int hl = warp + 2 * kWarps; hl < G; hl += kWarps) {  // G > 16: the rest one by one
+            float M = -INFINITY, sm = 0.f, mc = -INFINITY, sc_ = 0.f;
+            if (on) {
+              mc = __ldcg(&stat(lane, hl)->mx);
+              sc_ = __ldcg(&stat(lane, hl)->s);
+            }
+            M = pass == 0 ? warp_nanmax(mc) : misc->m[hl];
+            if (pass == 1) sm = sc_;
+            else if (fast16) sm = (sc_ == 0.f) ? 0.f : sc_ * __expf(mc - M);
+            sm = warp_sum(sm);
+            if (lane == 0) {
+              if (pass == 0) misc->m[hl] = M;
+              if (pass == 1 || fast16) misc->s[hl] = sm;
+            }
+          }
+        } else if (pass == 0 || !fast16) {
           for (int hl = warp; hl < G; hl += kWarps) {
             float M = -INFINITY;
             if (pass == 0) {
@@ -2493,10 +2552,13 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
             }
           }
         }
-        // the group's histograms of this pass into shared memory, all loads
-        // in flight together, then each head's bin from there
-        for (int i = threadIdx.x; i < G * 256; i += kThreads)
-          hsm[(i >> 8) * HS + (i & 255)] = __ldcg(&gh[(size_t)pass * G * 256 + i]);
+        // the group's histograms of this pass into shared memory, then each
+        // head's bin from there
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int i = threadIdx.x + k * kThreads;
+          if (i < G * 256) hsm[(i >> 8) * HS + (i & 255)] = hv[k];
+        }
         __syncthreads();
         for (int hl = warp; hl < G; hl += kWarps) {
           int above = 0;
@@ -2709,7 +2771,23 @@ __global__ void __launch_bounds__(kThreads, 1) saga_decode_kernel(const __grid_c
       // flight together): the total above pN, then in chunk order the ties
       // each chunk keeps, clamp(need - ties before it, 0, its ties), and the
       // rank of this chunk's first kept position.
-      for (int hl = warp; hl < G; hl += kWarps) {
+      for (int hl = warp; hl < G && C <= 32; hl += kWarps) {
+        // a lane per chunk, its two counts loaded once
+        const int cg = lane < C ? __ldcg(&stat(lane, hl)->cnt) : 0;
+        const int ce = lane < C ? __ldcg(&stat(lane, hl)->cnt_eq) : 0;
+        const int tot_gt = warp_sum_i(cg);
+        const int need = max(0, nsel - tot_gt);
+        const int ex = warp_incl_scan(ce) - ce;  // ties of the chunks before this lane's
+        const int before = lane < j ? 1 : 0;
+        const int pos_pre = warp_sum_i(before * (cg + max(0, min(ce, need - ex))));
+        const int eq_pre = warp_sum_i(before * ce);
+        if (lane == 0) {
+          misc->i2[hl] = max(0, min(misc->i2[hl], need - eq_pre));  // kept ties here
+          misc->i3[hl] = max(0, pos_pre);
+          if (jl == 0 && p.count_out) p.count_out[row0 + hl] = tot_gt;
+        }
+      }
+      for (int hl = warp; hl < G && C > 32; hl += kWarps) {
         int tot_gt = 0;
         for (int c0 = 0; c0 < C; c0 += 32) {
           const int c = c0 + lane;
