@@ -919,10 +919,16 @@ __device__ __forceinline__ bool bit_of(const uint32_t* bits, int i) { return (bi
 // or for calibration the probability rounded to the dtype.
 template <typename T, int MODE>
 __device__ __forceinline__ float weight_from_logit(float l, const Misc* misc, int hl) {
-  if constexpr (MODE == MODE_CALIBRATE)
+  if constexpr (MODE == MODE_CALIBRATE) {
     return Num<T>::round(__fdiv_rn(expf(__fsub_rn(l, misc->m[hl])), misc->s[hl]));
-  else
+  } else if constexpr (MODE == MODE_DENSE) {
+    // A chunk the mask covers whole has max -inf; its weights are 0, not
+    // exp(-inf - -inf). (Selected positions of the other modes are finite.)
+    const float a = misc->aux[hl];
+    return __expf(l - (a == -INFINITY ? 0.f : a));
+  } else {
     return __expf(l - misc->aux[hl]);
+  }
 }
 template <typename T, int MODE>
 __device__ __forceinline__ float weight_of(const T* sc, int SH, const Misc* misc, int hl, int i) {
@@ -1604,6 +1610,7 @@ __device__ void dense_stream_pv(const DecodeParams& p, int g, int j, int b, int 
     float ls[8];
 #pragma unroll
     for (int hh = 0; hh < 8; ++hh) ls[hh] = 0.f;
+    float stab[16];  // the group's stabilisers; 0 for a head the mask covers whole in this chunk
     for (int k = 0; k < nsteps; ++k) {
       const int gi = k / ntl, t = k - gi * ntl;
       const uint32_t u = vs0 + (uint32_t)k;
@@ -1615,13 +1622,19 @@ __device__ void dense_stream_pv(const DecodeParams& p, int g, int j, int b, int 
         break;
       }
       const int hb = misc->ghb[gi] & 0xFFFF, nh = misc->ghb[gi] >> 16;
+      if (t == 0) {
+#pragma unroll
+        for (int hh = 0; hh < 16; ++hh) {
+          const float a = hh < nh ? misc->aux[hb + hh] : 0.f;
+          stab[hh] = a == -INFINITY ? 0.f : a;
+        }
+      }
       const int pos = t * 128 + tid;
       uint8_t* wb = wpv + s2 * W_BYTES;
 #pragma unroll
       for (int hh = 0; hh < 16; ++hh) {
         T e = Num<T>::from_f(0.f);
-        if (hh < nh && pos < n)
-          e = Num<T>::from_f(__expf(Num<T>::to_f(sc[pos * SH + hb + hh]) - misc->aux[hb + hh]));
+        if (hh < nh && pos < n) e = Num<T>::from_f(__expf(Num<T>::to_f(sc[pos * SH + hb + hh]) - stab[hh]));
         *reinterpret_cast<T*>(wb + pv_w_off(tid, hh)) = e;
         if (hh < 8) ls[hh] += Num<T>::to_f(e);  // the rounded weight the MMA multiplies
       }
