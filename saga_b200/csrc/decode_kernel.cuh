@@ -57,7 +57,7 @@ struct Misc {
   uint32_t tmem_slot;
   int abort;
   uint32_t tag;                // exchange tag of this launch for the current group
-  int stored;                  // tiles x 4 epilogue warps stored to SMEM (this item)
+  int stored4[4];              // own tiles each epilogue warp stored to SMEM (this item)
   uint32_t tkey[kMaxG];        // order-preserving keys of the tail max (fp32 path)
   float ered[2][kMaxG];        // per-helper-warp partial exp-sums
   float emax[2][kMaxG];        // per-helper-warp partial maxima
@@ -526,7 +526,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
     *reinterpret_cast<uint4*>(qop + kb * 2048 + h * 128 + ((c ^ (h & 7)) << 4)) = *reinterpret_cast<uint4*>(vals);
   }
   if (threadIdx.x == 0) {
-    misc->stored = 0;
+    for (int k = 0; k < 4; ++k) misc->stored4[k] = 0;
     misc->mready = 0;
     misc->tcount = 0;
   }
@@ -702,7 +702,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       if (!pre && q - n_pre < 16 && q4 == 0 && lane == 0) trace_col(p, 48 + (q - n_pre), clock64());
       if (!pre && lane == 0) {
         __threadfence_block();
-        atomicAdd(&misc->stored, 1);
+        atomicAdd(&misc->stored4[q4], 1);
       }
       if (pre && q == n_pre - 1) {
         // tail max of the group: warp max, then the last of the four epilogue
@@ -769,10 +769,17 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
       s[hl] = 0.f;
       mx[hl] = -INFINITY;
     }
+    // Tile q is complete once each of the four epilogue warps stored its
+    // quarter: the warps may be a tile apart (two TMEM score buffers), so a
+    // total over the warps could count a later tile of one warp instead.
+    auto stored_min = [&]() {
+      const volatile int* s4 = misc->stored4;
+      return min(min(s4[0], s4[1]), min(s4[2], s4[3]));
+    };
     auto wait_stored = [&](int target) {
-      if (*reinterpret_cast<volatile int*>(&misc->stored) >= target) return true;
+      if (stored_min() >= target) return true;
       unsigned long long t0 = 0;
-      for (uint32_t it = 1; *reinterpret_cast<volatile int*>(&misc->stored) < target; ++it) {
+      for (uint32_t it = 1; stored_min() < target; ++it) {
         __nanosleep(64);
         if (misc->abort) return false;
         if ((it & 255u) == 0) {
@@ -817,7 +824,7 @@ __device__ void score_chunk_tc(const DecodeParams& p, int b, int kh, int p0, int
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) m2[jj] = PT::pack_rn(m[2 * jj], m[2 * jj + 1]);
     for (int q = 0; q < ntl && live; ++q) {
-      live = wait_stored(4 * (q + 1));
+      live = wait_stored(q + 1);
       if (!live) break;
       __threadfence_block();
 #pragma unroll
