@@ -41,3 +41,11 @@ def test_dropin_functions_refuse_host_tensors(fn):
             getattr(A, fn)(q, k, v, None)
     finally:
         A.AMORTIZED_THRESHOLD_TENSOR = saved
+
+
+@pytest.mark.parametrize("op", ["dense", "atopn", "calibrate"])
+def test_decode_step_refuses_host_tensors(op):
+    from saga_b200 import ops
+    q, k, v, thr = _inputs()
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.DecodeStep(op, q, k, v, threshold=thr, top_n=16)
